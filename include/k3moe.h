@@ -1,0 +1,175 @@
+/* k3moe — B200 (sm_100a) routed-MoE layer of Kimi-K3: the C ABI.
+ *
+ * Every entry takes caller-owned device buffers, plain pointers and sizes,
+ * and a CUDA stream; it enqueues work and returns 0, or a negative K3MOE_E*
+ * code for bad arguments or a launch failure.  Nothing here allocates device
+ * memory on the hot path; the layer entry carves its intermediates out of a
+ * caller-provided workspace (k3moe_layer_workspace_size).  Device-side
+ * failures (a routing-table entry out of range, a bounded wait that ran out)
+ * are written to the error words inside the workspace and read back with
+ * k3moe_read_error after the stream is synchronised; no kernel traps.
+ *
+ * Layouts (HBM):
+ *   activations x        bf16 [T, ldx]
+ *   router logits S      f32  [T, lds], E_total experts wide
+ *   expert weights       MXFP4: E2M1 two a byte (element 2i in the low nibble
+ *                        of byte i), rows of K/2 bytes; W13 of expert e is
+ *                        [gate rows 0..I-1 ; up rows I..2I-1] x H, W2 is H x I.
+ *                        Experts back to back: W13 [E, 2I, H/2], W2 [E, H, I/2].
+ *   weight scales        UE8M0 per 32 along K, 128x4-tiled over the
+ *                        flattened rows (byte of row r, group kb at
+ *                        ((r/128)*(K/128) + kb/4)*512 + (r%32)*16 + (r%128/32)*4 + kb%4).
+ *   MXFP8 activations    E4M3 bytes [rows, K] + UE8M0 per 32 along K, in the
+ *                        same tiled layout (linear [rows, K/32] where noted).
+ *   routing tables       the reference's format (docs/k3-kernel-abi.md K14,
+ *                        source/k3_moe_prefill.cu:12-35): cta_batch, cta_limit,
+ *                        num_non_exiting, total_padded, route_map, exp2perm.
+ */
+#ifndef K3MOE_H
+#define K3MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* k3moe_stream_t; /* a cudaStream_t */
+
+enum {
+  K3MOE_OK = 0,
+  K3MOE_EINVAL = -1,     /* an argument is out of the supported range */
+  K3MOE_ENOSPACE = -2,   /* workspace smaller than k3moe_layer_workspace_size */
+  K3MOE_EDRIVER = -3,    /* the CUDA driver entry for tensor maps is unavailable */
+  K3MOE_ETMAP = -4,      /* a tensor map could not be encoded (alignment / size) */
+  K3MOE_ELAUNCH = -5,    /* a kernel launch failed (cudaGetLastError) */
+  K3MOE_EDEVICE = -6     /* k3moe_read_error: the device reported a failure */
+};
+
+/* Version of this ABI. */
+int k3moe_abi_version(void);
+
+/* ---------------------------------------------------------------- router top-k
+ * sig = 1/(1+expf(-S)), key = sig + bias; the K largest keys, ties to the
+ * smaller expert, in descending order; wts = sig / (sum of the K sig + 1e-20)
+ * * rs, the sum an xor butterfly over the K picks.  K a power of two <= 16,
+ * E_total <= 1024.  Bit-identical to the reference's router top-k.
+ * Replaces: kern_k3g_router_topk (source/k3_prefill_glue.cu:504-557),
+ *   phase 1 of kern_k3g_moe_route (source/k3_moe_route.cu:117-221, 372-385). */
+int k3moe_route_topk(const float* S, int lds, const float* bias, const void* rs_bf16, int T, int E_total, int K,
+                     int32_t* idx, float* wts, k3moe_stream_t stream);
+
+/* ---------------------------------------------------------------- routing tables
+ * Over R rows with K ids each (global expert indices), the local experts being
+ * [first, first + E): counts[e], the CTA tables of `tile`-row tiles,
+ * meta[0] = num_non_exiting, meta[1] = total_padded, meta[2] = first permuted
+ * row of the shared expert (or -1), route_map[perm] = row (padding rows 0),
+ * exp2perm[r*K + k] = perm or -1 (foreign expert).  With shared = 1 a further
+ * local expert E takes every row.  Within an expert the rows are in row
+ * order, so the tables are the same bytes on every run.
+ * scratch: k3moe_route_scratch_bytes(R, E, shared) bytes.  E + shared <= 2048.
+ * Replaces: kern_k3_moe_route_count / _tables / _scatter
+ *   (source/k3_moe_prefill.cu:97-204), phase 2 of kern_k3g_moe_route
+ *   (source/k3_moe_route.cu:457-519), FlashInfer's routing offsets. */
+size_t k3moe_route_scratch_bytes(int R, int E, int shared);
+int k3moe_route_tables(const int32_t* idx, int R, int K, int first, int E, int shared, int tile, void* scratch,
+                       int32_t* counts, int32_t* cta_batch, int32_t* cta_limit, int32_t* meta, int32_t* route_map,
+                       int32_t* exp2perm, k3moe_stream_t stream);
+
+/* Capacity bounds of the tables: CTAs <= E + shared + ceil((R*K + shared*R) / tile). */
+int k3moe_max_ctas(int R, int K, int E, int shared, int tile);
+
+/* ---------------------------------------------------------------- MXFP8 quantisation
+ * Per 32 elements along a row: e = ceil(log2(amax/448)) (0 when amax is 0),
+ * clamped to [-127, 127]; sf = e + 127 (UE8M0); q = E4M3(x * 2^-e), round to
+ * nearest even, saturating.  cols a multiple of 256.
+ * tiled_sf = 0: sf linear [rows, cols/32]     (kern_k3_moe_quant, source/k3_moe_prefill.cu:66-95)
+ * tiled_sf = 1: sf in the 128x4-tiled layout  (kern_k3_mxfp8_quant, source/k3_mxfp8.cu:20-54) */
+int k3moe_quant_mxfp8(const void* x_bf16, int ldx, int rows, int cols, uint8_t* q, uint8_t* sf, int tiled_sf,
+                      k3moe_stream_t stream);
+
+/* The same quantisation written to every permuted row a row is routed to:
+ * q_perm [cap, cols], sf_perm tiled over permuted rows.  (The reference
+ * quantises unpermuted and gathers inside FC1; this build permutes here.) */
+int k3moe_quant_permute(const void* x_bf16, int ldx, int R, int cols, int K, const int32_t* exp2perm,
+                        const int32_t* meta, uint8_t* q_perm, uint8_t* sf_perm, k3moe_stream_t stream);
+
+/* ---------------------------------------------------------------- grouped GEMMs
+ * FC1: for every token tile c and 128 features f of its expert e:
+ *   g = W13_e[f] . x, u = W13_e[I + f] . x (block-scaled, f32 accumulate),
+ *   h = silu(g) * u, requantised to MXFP8 (the rule above) into
+ *   fc1_q [cap, I] / fc1_sf (tiled over permuted rows).
+ * FC2: fc2 [cap, H] bf16 = W2_e . fc1 over each tile's rows.
+ * Tables from k3moe_route_tables (tile 128).  H, I multiples of 256; err:
+ * the device error words (2 x u32).
+ * Replaces: the FC1 / FC2 batched GEMMs (kernels.toml:1-9; arguments
+ *   scripts/k3_moe_bmm.py:131-134, 167-169; docs/k3-kernel-abi.md:535-565). */
+int k3moe_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
+              const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* fc1_q,
+              uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
+              k3moe_stream_t stream);
+int k3moe_fc2(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+              const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, void* fc2_bf16, int H, int I,
+              int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream);
+
+/* ---------------------------------------------------------------- combine
+ * out[t] = bf16( sum over k = 0..K-1 with exp2perm >= 0 of fma(wts, fc2[p], acc)
+ * in f32, k in order, then + fc2[meta[2] + t] when meta and meta[2] >= 0 );
+ * rows t in [T, out_rows) are zero.  cols a multiple of 8.
+ * Replaces: kern_k3_moe_finalize (source/k3_moe_prefill.cu:206-234). */
+int k3moe_combine(const void* fc2_bf16, const int32_t* exp2perm, const float* wts, const int32_t* meta, void* out_bf16,
+                  int ldo, int T, int out_rows, int K, int cols, k3moe_stream_t stream);
+
+/* ---------------------------------------------------------------- weights
+ * fp32 [rows, K] -> MXFP4 (OCP MX: scale 2^(floor(log2 amax) - 2), RNE to
+ * E2M1, saturate at 6); packed [rows, K/2], scales tiled (see top).
+ * No reference counterpart: the reference consumes pre-quantised checkpoints. */
+int k3moe_quant_mxfp4(const float* w, long long rows, int K, uint8_t* packed, uint8_t* sf, k3moe_stream_t stream);
+/* Synthetic weights of stream `seed` (rows [row0, row0+rows)), quantised as above. */
+int k3moe_synth_mxfp4(uint64_t seed, long long row0, long long rows, int K, float sd, uint8_t* packed, uint8_t* sf,
+                      k3moe_stream_t stream);
+
+/* ---------------------------------------------------------------- the layer
+ * One routed-MoE layer on the experts this GPU holds: top-k -> tables ->
+ * MXFP8 permute -> FC1 -> FC2 -> combine (+ the shared expert, stored as
+ * local expert E of the weight tensors, applied to every row with weight 1).
+ * Replaces the chain of scripts/k3_moe_bmm.py:150-170 (route, fc1, fc2,
+ * finalize) for one rank holding every expert. */
+typedef struct k3moe_layer_args {
+  int T;              /* rows this call routes */
+  int H, I;           /* hidden, expert intermediate (multiples of 256) */
+  int E;              /* routed experts (= router width) */
+  int K;              /* top-k */
+  int shared;         /* 1: expert E of the weights is the always-on shared expert */
+  const float* S;     /* router logits f32 [T, lds] */
+  int lds;
+  const float* bias;  /* f32 [E] */
+  const void* rs;     /* bf16 [1] routed scale */
+  const void* x;      /* bf16 [T, ldx] */
+  int ldx;
+  const uint8_t* w13; const uint8_t* w13_sf;  /* [E + shared, 2I, H/2] */
+  const uint8_t* w2;  const uint8_t* w2_sf;   /* [E + shared, H, I/2] */
+  void* out;          /* bf16 [T, ldo] */
+  int ldo;
+} k3moe_layer_args;
+
+size_t k3moe_layer_workspace_size(int T, int H, int I, int E, int K, int shared);
+int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream);
+
+/* Intermediates of the last k3moe_layer_forward inside `workspace`, for
+ * inspection and tests: byte offsets of idx, wts, counts, cta_batch,
+ * cta_limit, meta, route_map, exp2perm, q_perm, sf_perm, fc1_q, fc1_sf, fc2,
+ * err (14 entries). */
+int k3moe_layer_workspace_offsets(int T, int H, int I, int E, int K, int shared, size_t* offsets14);
+
+/* Read (and clear, when clear != 0) the two device error words at `err`:
+ * returns 0 when both are zero, else K3MOE_EDEVICE with the words in out2.
+ * Synchronises `stream`. */
+int k3moe_read_error(uint32_t* err, uint32_t* out2, int clear, k3moe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* K3MOE_H */

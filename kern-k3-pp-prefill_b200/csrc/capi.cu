@@ -1,0 +1,354 @@
+// Host side of the k3moe C ABI (include/k3moe.h): argument checks, launch
+// geometry, TMA tensor-map encoding and the layer chain.  One translation unit
+// holds every kernel so the library needs no relocatable device code.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/k3moe.h"
+#include "gemm.cu"
+#include "route.cu"
+
+using namespace k3;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+int num_sms(int dev) {
+  static int cache[kMaxDevices] = {0};
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+// Kernel attributes are per device: set them once per (device, kernel).
+template <typename F>
+bool set_smem_once(F kernel, int bytes, int slot) {
+  static std::mutex mu;
+  static bool done[kMaxDevices][8] = {};
+  const int dev = current_device();
+  std::lock_guard<std::mutex> g(mu);
+  if (dev >= 0 && dev < kMaxDevices && done[dev][slot]) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (dev >= 0 && dev < kMaxDevices) done[dev][slot] = true;
+  return true;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major operand map: rows of `k` elements, a 128 x 128-element box, 128-byte swizzle.
+int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool fp4) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return K3MOE_EDRIVER;
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? k / 2 : k)};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? K3MOE_OK : K3MOE_ETMAP;
+}
+
+int launch_status() { return cudaGetLastError() == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH; }
+
+inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+template <int EPL>
+void launch_topk(const float* S, int lds, const float* bias, const bf16* rs, int T, int E, int K, int* idx,
+                 float* wts, cudaStream_t s) {
+  const int warps = 8;
+  const long long blocks = cdiv(T, warps);
+  topk_kernel<EPL><<<(unsigned)blocks, warps * 32, 0, s>>>(S, lds, bias, rs, T, E, K, idx, wts);
+}
+
+int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* act, const uint8_t* act_sf,
+                const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* out_q,
+                uint8_t* out_sf, void* out_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas,
+                uint32_t* err, cudaStream_t stream) {
+  if (H <= 0 || I <= 0 || H % 256 || I % 256 || n_experts <= 0 || cap_rows <= 0 || cap_rows % 128 || max_ctas <= 0 ||
+      (long long)max_ctas * 128 > cap_rows)
+    return K3MOE_EINVAL;
+  const int K = mode == MODE_FC1 ? H : I;
+  const int rows_per_expert = mode == MODE_FC1 ? 2 * I : H;
+  CUtensorMap ta, tb;
+  int rc = encode_operand(&ta, w, (long long)n_experts * rows_per_expert, K, true);
+  if (rc) return rc;
+  rc = encode_operand(&tb, act, cap_rows, K, false);
+  if (rc) return rc;
+  GemmParams p;
+  p.sfa = w_sf;
+  p.sfb = act_sf;
+  p.cta_batch = cta_batch;
+  p.cta_limit = cta_limit;
+  p.meta = meta;
+  p.out_q = out_q;
+  p.out_sf = out_sf;
+  p.out_bf16 = reinterpret_cast<bf16*>(out_bf16);
+  p.err = err;
+  p.K = K;
+  p.rows_per_expert = rows_per_expert;
+  p.n_experts = n_experts;
+  p.nfb = mode == MODE_FC1 ? I / gemm::BM : H / (gemm::BM * gemm::NACC);
+  p.out_cols = mode == MODE_FC1 ? I : H;
+  p.cap_rows = cap_rows;
+  p.max_ctas = max_ctas;
+  const long long max_units = (long long)max_ctas * p.nfb;
+  const int grid = (int)std::min<long long>(num_sms(current_device()), max_units);
+  if (mode == MODE_FC1) {
+    if (!set_smem_once(grouped_gemm_kernel<MODE_FC1>, gemm::SMEM_BYTES, 0)) return K3MOE_ELAUNCH;
+    grouped_gemm_kernel<MODE_FC1><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
+  } else {
+    if (!set_smem_once(grouped_gemm_kernel<MODE_FC2>, gemm::SMEM_BYTES, 1)) return K3MOE_ELAUNCH;
+    grouped_gemm_kernel<MODE_FC2><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
+  }
+  return launch_status();
+}
+
+struct LayerLayout {
+  size_t off[14];
+  size_t total;
+  int max_ctas, cap_rows, nb, EL;
+  size_t blockcount, blockoff;  // inside the route scratch
+};
+
+enum { L_IDX, L_WTS, L_COUNTS, L_CTA_BATCH, L_CTA_LIMIT, L_META, L_ROUTE_MAP, L_EXP2PERM, L_QP, L_SFP, L_FC1Q,
+       L_FC1SF, L_FC2, L_ERR };
+
+LayerLayout layer_layout(int T, int H, int I, int E, int K, int shared) {
+  LayerLayout L;
+  L.EL = E + shared;
+  L.nb = (int)cdiv(T, TB);
+  L.max_ctas = k3moe_max_ctas(T, K, E, shared, 128);
+  L.cap_rows = L.max_ctas * 128;
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = at;
+    at = align_up(at + bytes, 1024);
+    return o;
+  };
+  L.off[L_IDX] = take((size_t)T * K * 4);
+  L.off[L_WTS] = take((size_t)T * K * 4);
+  L.off[L_COUNTS] = take((size_t)L.EL * 4);
+  L.off[L_CTA_BATCH] = take((size_t)L.max_ctas * 4);
+  L.off[L_CTA_LIMIT] = take((size_t)L.max_ctas * 4);
+  L.off[L_META] = take(16);
+  L.off[L_ROUTE_MAP] = take((size_t)L.cap_rows * 4);
+  L.off[L_EXP2PERM] = take((size_t)T * K * 4);
+  L.off[L_QP] = take((size_t)L.cap_rows * H);
+  L.off[L_SFP] = take((size_t)L.cap_rows * H / 32);
+  L.off[L_FC1Q] = take((size_t)L.cap_rows * I);
+  L.off[L_FC1SF] = take((size_t)L.cap_rows * I / 32);
+  L.off[L_FC2] = take((size_t)L.cap_rows * H * 2);
+  L.off[L_ERR] = take(16);
+  L.blockcount = take((size_t)L.nb * L.EL * 4);
+  L.blockoff = take((size_t)L.nb * L.EL * 4);
+  L.total = at;
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int k3moe_abi_version(void) { return 1; }
+
+int k3moe_route_topk(const float* S, int lds, const float* bias, const void* rs_bf16, int T, int E_total, int K,
+                     int32_t* idx, float* wts, k3moe_stream_t stream) {
+  if (T < 0 || E_total < K || E_total > 1024 || K < 1 || K > 16 || (K & (K - 1)) || lds < E_total) return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bf16* rs = reinterpret_cast<const bf16*>(rs_bf16);
+  const int epl = (E_total + 31) / 32;
+  if (epl <= 1) launch_topk<1>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  else if (epl <= 2) launch_topk<2>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  else if (epl <= 4) launch_topk<4>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  else if (epl <= 8) launch_topk<8>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  else if (epl <= 16) launch_topk<16>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  else if (epl <= 28) launch_topk<28>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  else launch_topk<32>(S, lds, bias, rs, T, E_total, K, idx, wts, s);
+  return launch_status();
+}
+
+int k3moe_max_ctas(int R, int K, int E, int shared, int tile) {
+  if (R < 0 || K < 1 || E < 1 || tile < 1) return 0;
+  const long long rows = (long long)R * K + (long long)(shared ? R : 0);
+  return (int)(E + (shared ? 1 : 0) + cdiv(rows, tile));
+}
+
+size_t k3moe_route_scratch_bytes(int R, int E, int shared) {
+  const size_t nb = (size_t)cdiv(R, TB);
+  return 2 * align_up(nb * (E + (shared ? 1 : 0)) * 4, 256);
+}
+
+int k3moe_route_tables(const int32_t* idx, int R, int K, int first, int E, int shared, int tile, void* scratch,
+                       int32_t* counts, int32_t* cta_batch, int32_t* cta_limit, int32_t* meta, int32_t* route_map,
+                       int32_t* exp2perm, k3moe_stream_t stream) {
+  shared = shared ? 1 : 0;
+  if (R < 1 || K < 1 || K > 16 || E < 1 || E + shared > 2048 || tile < 8 || tile > 1024) return K3MOE_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int nb = (int)cdiv(R, TB), EL = E + shared;
+  int* blockcount = reinterpret_cast<int*>(scratch);
+  int* blockoff = reinterpret_cast<int*>(reinterpret_cast<char*>(scratch) + align_up((size_t)nb * EL * 4, 256));
+  route_count_kernel<<<nb, TB, EL * 4, s>>>(idx, R, K, first, E, shared, blockcount, nullptr);
+  route_tables_kernel<<<1, 1024, 0, s>>>(blockcount, nb, E, shared, tile, blockoff, counts, cta_batch, cta_limit, meta,
+                                         route_map);
+  const int sc_smem = E * (TB / 32) * 4;
+  if (sc_smem > 48 * 1024 && !set_smem_once(route_scatter_kernel, sc_smem, 2)) return K3MOE_ELAUNCH;
+  route_scatter_kernel<<<nb, TB, sc_smem, s>>>(idx, R, K, first, E, shared, blockoff, route_map, exp2perm);
+  return launch_status();
+}
+
+int k3moe_quant_mxfp8(const void* x_bf16, int ldx, int rows, int cols, uint8_t* q, uint8_t* sf, int tiled_sf,
+                      k3moe_stream_t stream) {
+  if (rows < 0 || cols <= 0 || cols % 256 || ldx < cols || ldx % 8) return K3MOE_EINVAL;
+  if (rows == 0) return K3MOE_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long pieces = (long long)rows * (cols / 256);
+  const int grid = (int)std::min<long long>(cdiv(pieces, 8), (long long)num_sms(current_device()) * 16);
+  const bf16* x = reinterpret_cast<const bf16*>(x_bf16);
+  if (tiled_sf) quant_tiled_kernel<<<grid, 256, 0, s>>>(x, ldx, rows, cols, q, sf);
+  else quant_linear_kernel<<<grid, 256, 0, s>>>(x, ldx, rows, cols, q, sf);
+  return launch_status();
+}
+
+int k3moe_quant_permute(const void* x_bf16, int ldx, int R, int cols, int K, const int32_t* exp2perm,
+                        const int32_t* meta, uint8_t* q_perm, uint8_t* sf_perm, k3moe_stream_t stream) {
+  if (R < 0 || cols <= 0 || cols % 256 || ldx < cols || ldx % 8 || K < 1 || K > 16) return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int grid = (int)std::min<long long>(cdiv(R, 8), (long long)num_sms(current_device()) * 8);
+  quant_permute_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x_bf16), ldx, R, cols, K, exp2perm, meta,
+                                            q_perm, sf_perm);
+  return launch_status();
+}
+
+int k3moe_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
+              const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* fc1_q,
+              uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
+              k3moe_stream_t stream) {
+  return gemm_launch(MODE_FC1, w13, w13_sf, q_perm, sf_perm, cta_batch, cta_limit, meta, fc1_q, fc1_sf, nullptr, H, I,
+                     n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int k3moe_fc2(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+              const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, void* fc2_bf16, int H, int I,
+              int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream) {
+  return gemm_launch(MODE_FC2, w2, w2_sf, fc1_q, fc1_sf, cta_batch, cta_limit, meta, nullptr, nullptr, fc2_bf16, H, I,
+                     n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int k3moe_combine(const void* fc2_bf16, const int32_t* exp2perm, const float* wts, const int32_t* meta, void* out_bf16,
+                  int ldo, int T, int out_rows, int K, int cols, k3moe_stream_t stream) {
+  if (T < 0 || out_rows < T || K < 1 || K > 16 || cols <= 0 || cols % 8 || ldo < cols || ldo % 8) return K3MOE_EINVAL;
+  if (out_rows == 0) return K3MOE_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  combine_kernel<<<out_rows, 256, 0, s>>>(reinterpret_cast<const bf16*>(fc2_bf16), exp2perm, wts, meta,
+                                          reinterpret_cast<bf16*>(out_bf16), ldo, T, K, cols);
+  return launch_status();
+}
+
+int k3moe_quant_mxfp4(const float* w, long long rows, int K, uint8_t* packed, uint8_t* sf, k3moe_stream_t stream) {
+  if (rows < 0 || K <= 0 || K % 128) return K3MOE_EINVAL;
+  if (rows == 0) return K3MOE_OK;
+  const long long groups = rows * (K / 32);
+  const int grid = (int)std::min<long long>(cdiv(groups, 256), (long long)num_sms(current_device()) * 32);
+  quant_mxfp4_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(w, rows, K, packed, sf);
+  return launch_status();
+}
+
+int k3moe_synth_mxfp4(uint64_t seed, long long row0, long long rows, int K, float sd, uint8_t* packed, uint8_t* sf,
+                      k3moe_stream_t stream) {
+  if (rows < 0 || row0 < 0 || K <= 0 || K % 128 || row0 % 128) return K3MOE_EINVAL;
+  if (rows == 0) return K3MOE_OK;
+  const long long groups = rows * (K / 32);
+  const int grid = (int)std::min<long long>(cdiv(groups, 256), (long long)num_sms(current_device()) * 32);
+  // the tiled scale offsets are relative to row0 (a multiple of 128): callers pass sf at row0's atom
+  synth_mxfp4_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(seed, row0, rows, K, sd, packed, sf);
+  return launch_status();
+}
+
+size_t k3moe_layer_workspace_size(int T, int H, int I, int E, int K, int shared) {
+  if (T < 1 || H < 256 || I < 256 || E < 1 || K < 1) return 0;
+  return layer_layout(T, H, I, E, K, shared ? 1 : 0).total;
+}
+
+int k3moe_layer_workspace_offsets(int T, int H, int I, int E, int K, int shared, size_t* offsets14) {
+  if (T < 1 || H < 256 || I < 256 || E < 1 || K < 1 || !offsets14) return K3MOE_EINVAL;
+  const LayerLayout L = layer_layout(T, H, I, E, K, shared ? 1 : 0);
+  for (int i = 0; i < 14; ++i) offsets14[i] = L.off[i];
+  return K3MOE_OK;
+}
+
+int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream) {
+  if (!a || !workspace) return K3MOE_EINVAL;
+  const int shared = a->shared ? 1 : 0;
+  if (a->T < 1 || a->H % 256 || a->I % 256 || a->E < a->K || a->E > 1024 || a->ldx < a->H || a->ldo < a->H)
+    return K3MOE_EINVAL;
+  const LayerLayout L = layer_layout(a->T, a->H, a->I, a->E, a->K, shared);
+  if (ws_bytes < L.total) return K3MOE_ENOSPACE;
+  char* ws = reinterpret_cast<char*>(workspace);
+  auto I32 = [&](int i) { return reinterpret_cast<int32_t*>(ws + L.off[i]); };
+  auto U8 = [&](int i) { return reinterpret_cast<uint8_t*>(ws + L.off[i]); };
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws + L.off[L_ERR]);
+  if (cudaMemsetAsync(err, 0, 8, s) != cudaSuccess) return K3MOE_ELAUNCH;
+  float* wts = reinterpret_cast<float*>(ws + L.off[L_WTS]);
+  int rc = k3moe_route_topk(a->S, a->lds, a->bias, a->rs, a->T, a->E, a->K, I32(L_IDX), wts, stream);
+  if (rc) return rc;
+  // the route scratch (block counts / offsets) sits at the end of the layout
+  rc = k3moe_route_tables(I32(L_IDX), a->T, a->K, 0, a->E, shared, 128, ws + L.blockcount, I32(L_COUNTS),
+                          I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META), I32(L_ROUTE_MAP), I32(L_EXP2PERM), stream);
+  if (rc) return rc;
+  rc = k3moe_quant_permute(a->x, a->ldx, a->T, a->H, a->K, I32(L_EXP2PERM), I32(L_META), U8(L_QP), U8(L_SFP), stream);
+  if (rc) return rc;
+  const int nexp = a->E + shared;
+  rc = k3moe_fc1(a->w13, a->w13_sf, U8(L_QP), U8(L_SFP), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META), U8(L_FC1Q),
+                 U8(L_FC1SF), a->H, a->I, nexp, L.cap_rows, L.max_ctas, err, stream);
+  if (rc) return rc;
+  rc = k3moe_fc2(a->w2, a->w2_sf, U8(L_FC1Q), U8(L_FC1SF), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META),
+                 ws + L.off[L_FC2], a->H, a->I, nexp, L.cap_rows, L.max_ctas, err, stream);
+  if (rc) return rc;
+  return k3moe_combine(ws + L.off[L_FC2], I32(L_EXP2PERM), wts, I32(L_META), a->out, a->ldo, a->T, a->T, a->K, a->H,
+                       stream);
+}
+
+int k3moe_read_error(uint32_t* err, uint32_t* out2, int clear, k3moe_stream_t stream) {
+  if (!err || !out2) return K3MOE_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(out2, err, 8, cudaMemcpyDeviceToHost, s) != cudaSuccess) return K3MOE_ELAUNCH;
+  if (clear && cudaMemsetAsync(err, 0, 8, s) != cudaSuccess) return K3MOE_ELAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return K3MOE_ELAUNCH;
+  return (out2[0] | out2[1]) ? K3MOE_EDEVICE : K3MOE_OK;
+}
+
+}  // extern "C"

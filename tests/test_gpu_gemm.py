@@ -1,0 +1,104 @@
+"""GPU parity of the tcgen05 grouped GEMMs and of the whole layer against the
+CPU fp32 dequantise-and-matmul oracle, through the C ABI.
+
+Tolerances: relative L2 <= 1e-2 and, per element, max(2e-2, 3 bf16 ulp + 1e-3)
+(the contract's max-abs, widened to the reference harness's element bound
+where one bf16 step of a large output exceeds 2e-2; see cases.within_contract).  The FC1 output is MXFP8, so it is compared after dequantising;
+a requantised element may land one E4M3 step away where the two sides' f32
+accumulations straddle a rounding boundary."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+import k3moe
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _stage_inputs(c, dev):
+    idx, wts = oracle.topk(c.S, c.bias, c.rs_bits, c.K)
+    tb = oracle.tables(idx, c.E, 0, c.shared)
+    qp, sfp = oracle.quant_permute(c.x_bits, tb["exp2perm"], tb["meta"], tb["cap_rows"])
+    t = k3moe.route_tables(_t(idx, dev), c.E, 0, c.shared)
+    return idx, wts, tb, qp, sfp, t
+
+
+def _rows_of(tb):
+    nne = int(tb["meta"][0])
+    rows = []
+    for cidx in range(nne):
+        rows.extend(range(cidx * 128, int(tb["cta_limit"][cidx])))
+    return np.array(rows, np.int64)
+
+
+@pytest.mark.parametrize("cfg", [dict(T=128, H=1024, I=512, E=16, K=4, shared=0),
+                                 dict(T=200, H=1024, I=512, E=8, K=4, shared=1),
+                                 dict(T=64, H=2048, I=256, E=4, K=2, shared=0)])
+def test_fc1_fc2_against_oracle(dev, cfg):
+    c = cases.make_case(**cfg, rs=1.0, seed=1)
+    idx, wts, tb, qp, sfp, t = _stage_inputs(c, dev)
+    g = cases.to_device(c, dev)
+    err = torch.zeros(4, dtype=torch.int32, device=dev)
+    ne = c.E + c.shared
+    f1q, f1sf = k3moe.fc1(g["w13"], g["w13_sf"], _t(qp, dev), _t(sfp, dev), t, c.H, c.I, ne, err)
+    torch.cuda.synchronize()
+    assert err.cpu().numpy()[:2].tolist() == [0, 0]
+    nne = int(tb["meta"][0])
+    ref_q, ref_sf = oracle.fc1(c.w13, c.w13_sf, qp, sfp, tb["cta_batch"], tb["cta_limit"], 0, nne, c.H, c.I)
+    rows = _rows_of(tb)
+    got = oracle.dequant_rows(f1q.cpu().numpy(), f1sf.cpu().numpy(), rows)
+    ref = oracle.dequant_rows(ref_q, ref_sf, rows)
+    rel = cases.rel_l2(got, ref)
+    assert rel <= 2e-2, f"fc1 rel-L2 {rel:.3e}"
+    # FC2 from the device's own FC1 output, against the oracle's FC2 of those same bytes
+    y = k3moe.fc2(g["w2"], g["w2_sf"], f1q, f1sf, t, c.H, c.I, ne, err)
+    torch.cuda.synchronize()
+    assert err.cpu().numpy()[:2].tolist() == [0, 0]
+    ref_y = oracle.fc2(c.w2, c.w2_sf, f1q.cpu().numpy(), f1sf.cpu().numpy(), tb["cta_batch"], tb["cta_limit"], 0, nne,
+                       c.H, c.I)
+    gy = y.float().cpu().numpy()[rows]
+    ry = oracle.bf16_to_f32(ref_y[rows])
+    ok, rel, ratio = cases.within_contract(gy, ry)
+    assert ok, f"fc2 rel-L2 {rel:.3e}, worst element at {ratio:.2f}x its bound"
+
+
+@pytest.mark.parametrize("cfg", [dict(T=128, H=1024, I=512, E=16, K=4, shared=0, rs=1.0),
+                                 dict(T=333, H=1024, I=512, E=32, K=8, shared=1, rs=2.5),
+                                 dict(T=64, H=7168, I=2048, E=8, K=8, shared=1, rs=2.5)])
+def test_layer_against_oracle(dev, cfg):
+    c = cases.make_case(**cfg, seed=2)
+    ref_out, inter = cases.oracle_forward(c)
+    g = cases.to_device(c, dev)
+    layer = k3moe.MoELayer(c.H, c.I, c.E, c.K, c.shared, g["w13"], g["w13_sf"], g["w2"], g["w2_sf"], g["bias"],
+                           g["rs"], max_tokens=c.T, device=dev)
+    out = layer.forward(g["S"], g["x"])
+    torch.cuda.synchronize()
+    layer.check_device_error(c.T)
+    got = out.float().cpu().numpy()
+    ref = oracle.bf16_to_f32(ref_out)
+    ok, rel, ratio = cases.within_contract(got, ref)
+    assert ok, f"layer rel-L2 {rel:.3e}, worst element at {ratio:.2f}x its bound"
+    # the routing and quantisation stages inside the layer are bit-exact
+    off = layer.offsets(c.T)
+    ws = layer.ws.cpu().numpy()
+    idx = ws[off["idx"]:off["idx"] + c.T * c.K * 4].view(np.int32).reshape(c.T, c.K)
+    assert np.array_equal(idx, inter["idx"])
+    e2p = ws[off["exp2perm"]:off["exp2perm"] + c.T * c.K * 4].view(np.int32).reshape(c.T, c.K)
+    assert np.array_equal(e2p, inter["tables"]["exp2perm"])
+
+
+def test_layer_repeatable(dev):
+    c = cases.make_case(T=256, H=1024, I=512, E=16, K=4, shared=1, rs=2.5, seed=3)
+    g = cases.to_device(c, dev)
+    layer = k3moe.MoELayer(c.H, c.I, c.E, c.K, c.shared, g["w13"], g["w13_sf"], g["w2"], g["w2_sf"], g["bias"],
+                           g["rs"], max_tokens=c.T, device=dev)
+    a = layer.forward(g["S"], g["x"]).clone()
+    b = layer.forward(g["S"], g["x"]).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16)), "the layer is not deterministic"
