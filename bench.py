@@ -1,0 +1,428 @@
+"""Benchmark of the Kimi-K3 routed-MoE layer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl k3moe|reference]
+
+A step is one MoE layer over an 8192-row prefill chunk: router top-k ->
+routing tables -> MXFP8 permute -> FC1 (MXFP8 x MXFP4, SwiGLU, MXFP8 out) ->
+FC2 (bf16) -> routing-weighted combine, plus the always-on shared expert.
+Shapes: T=8192 (16 packed sequences, Dirichlet lengths), H=7168, I=2048,
+E=896 routed experts, top-8, routed scale 2.5, shared expert width 2048; all
+expert weights MXFP4 (20.96 GB), synthetic and seeded (no checkpoint, no
+dataset).  The router logits S = x.W_router are computed once before timing
+(the router GEMM is the layer before this path).
+
+`value` is device-resident throughput (tokens/s over all ranks); `e2e` is the
+same layer through the public API with x and S copied from pinned host memory
+and the output copied back inside every timed step.  With N > 1 every rank
+runs its own 8192-row chunk through all 896 experts (the experts replicated
+per GPU, no data-path collective; weak scaling).  `--impl reference` times the
+CPU restatement of the same path (oracle/, the reference's algorithm) on a
+bounded sample on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "kern-k3-pp-prefill_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "MoE layer tokens/s @8192-row prefill"
+T_DEF, H, I, E, K, SHARED, RS = 8192, 7168, 2048, 896, 8, 1, 2.5
+W_SEED13, W_SEED2, WSD = 11, 12, 0.02
+FP8_PEAK_TFLOPS = 4500.0  # dense FP8 / MXF8F6F4 nominal (no measured figure for this kind exists here)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cu_seqlens(T, n=16, seed=0):
+    rng = np.random.default_rng(seed)
+    w = rng.dirichlet(np.ones(n))
+    lens = np.maximum(1, np.floor(w * T).astype(np.int64))
+    lens[-1] = T - lens[:-1].sum()
+    return np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+
+
+def layer_flops(T):
+    return 6.0 * H * I * (T * K + SHARED * T)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """NVML samples of SM clock and throttle reasons while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, uuid):
+        self.samples, self.reasons, self.ok = [], set(), False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as ex:  # no NVML: the line says so
+            self.err = str(ex)
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                get = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                r = get(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": f"NVML unavailable: {self.err}"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle port)
+def cpu_sample(sample_tiles, tb, wsrc, qsrc, threads=0):
+    """Time the oracle's FC1 + FC2 over `sample_tiles` token tiles (compact copies).
+
+    tb: host tables (cta_batch, cta_limit); wsrc(e) -> (w13, w13_sf, w2, w2_sf) of expert e;
+    qsrc(c) -> (q rows [128, H], tiled sf of the tile).  Returns seconds."""
+    import oracle
+
+    oracle.set_threads(threads)
+    ns = len(sample_tiles)
+    kg4 = H // 128
+    qp = np.zeros((ns * 128, H), np.uint8)
+    sfp = np.zeros(ns * kg4 * 512, np.uint8)
+    w13 = np.zeros((ns * 2 * I, H // 2), np.uint8)
+    w13sf = np.zeros(ns * 2 * I // 128 * kg4 * 512, np.uint8)
+    w2 = np.zeros((ns * H, I // 2), np.uint8)
+    w2sf = np.zeros(ns * H // 128 * (I // 128) * 512, np.uint8)
+    cb = np.arange(ns, dtype=np.int32)
+    cl = np.zeros(ns, np.int32)
+    for i, c in enumerate(sample_tiles):
+        e = int(tb["cta_batch"][c])
+        n = int(tb["cta_limit"][c]) - c * 128
+        cl[i] = i * 128 + n
+        q, sf = qsrc(c)
+        qp[i * 128:(i + 1) * 128] = q
+        sfp[i * kg4 * 512:(i + 1) * kg4 * 512] = sf
+        a, asf, b, bsf = wsrc(e)
+        w13[i * 2 * I:(i + 1) * 2 * I] = a
+        w13sf[i * len(asf):(i + 1) * len(asf)] = asf
+        w2[i * H:(i + 1) * H] = b
+        w2sf[i * len(bsf):(i + 1) * len(bsf)] = bsf
+    t0 = time.perf_counter()
+    f1q, f1sf = oracle.fc1(w13, w13sf, qp, sfp, cb, cl, 0, ns, H, I)
+    oracle.fc2(w2, w2sf, f1q, f1sf, cb, cl, 0, ns, H, I)
+    return time.perf_counter() - t0
+
+
+def cpu_topk_time(S, bias, rs_bits):
+    import oracle
+
+    t0 = time.perf_counter()
+    oracle.topk(S, bias, rs_bits, K)
+    return time.perf_counter() - t0
+
+
+def sample_tiles_of(nne, n=16):
+    return sorted(set(np.linspace(0, nne - 1, n).astype(int).tolist()))
+
+
+# ------------------------------------------------------------------ the reference arm (CPU)
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    threads = oracle.set_threads(0)
+    T = args.tokens
+    rng = np.random.default_rng(0)
+    x_bits = oracle.bf16_bits(rng.standard_normal((T, H), dtype=np.float32))
+    wr = (rng.standard_normal((H, E), dtype=np.float32) / np.sqrt(H)).astype(np.float32)
+    S = (oracle.bf16_to_f32(x_bits) @ wr).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, E).astype(np.float32)
+    rs_bits = int(oracle.bf16_bits(np.array([RS], np.float32))[0])
+    idx, wts = oracle.topk(S, bias, rs_bits, K)
+    tb = oracle.tables(idx, E, 0, SHARED)
+    nne = int(tb["meta"][0])
+    tiles = sample_tiles_of(nne, args.cpu_tiles)
+    wcache = {}
+
+    def wsrc(e):
+        if e not in wcache:
+            a = oracle.synth_f32(W_SEED13, 2 * I, H, WSD, row0=e * 2 * I)
+            b = oracle.synth_f32(W_SEED2, H, I, WSD, row0=e * H)
+            wcache[e] = oracle.quant_mxfp4(a) + oracle.quant_mxfp4(b)
+        return wcache[e]
+
+    def qsrc(c):
+        rows = tb["route_map"][c * 128:(c + 1) * 128]
+        q, sf = oracle.quant_mxfp8(x_bits[rows], tiled=True)
+        return q, sf
+
+    for e in {int(tb["cta_batch"][c]) for c in tiles}:
+        wsrc(e)
+    times = []
+    for step in range(args.warmup + args.steps):
+        t = cpu_topk_time(S, bias, rs_bits) + cpu_sample(tiles, tb, wsrc, qsrc, threads) * nne / len(tiles)
+        if step >= args.warmup:
+            times.append(t)
+    sec = statistics.mean(times)
+    value = T / sec
+    sample = (f"router top-k over all {T} rows + oracle FC1+FC2 over {len(tiles)} of {nne} token tiles (spread "
+              f"evenly), scaled by {nne}/{len(tiles)}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
+        "config": {"workload": "K3-shape prefill MoE layer (config 1)", "T": T, "H": H, "I": I, "E": E, "K": K,
+                   "shared": SHARED, "rs": RS},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ the GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="k3moe", choices=["k3moe", "reference"])
+    ap.add_argument("--tokens", type=int, default=T_DEF)
+    ap.add_argument("--experts", type=int, default=896, help="routed experts (smaller only for profiling captures)")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="e2e steps (default: --steps)")
+    ap.add_argument("--cpu-tiles", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import k3moe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    E = args.experts  # noqa: N806  (the routed experts of this run; smaller only for profiling captures)
+    T = args.tokens
+    k3moe.lib()
+
+    # weights: [gate; up] rows of every routed expert then the shared expert (expert E)
+    ne = E + SHARED
+    w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, ne * 2 * I, H, WSD, device=dev)
+    w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, ne * H, I, WSD, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn((T, H), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    g.manual_seed(7)
+    wr = torch.randn((H, E), generator=g, device=dev, dtype=torch.float32) / H ** 0.5
+    S = (x.float() @ wr).contiguous()
+    bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
+    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
+    del wr
+    layer = k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    for _ in range(args.warmup):
+        layer.forward(S, x, out)
+    torch.cuda.synchronize()
+    layer.check_device_error(T)
+
+    # ---------------- device-resident timing, per-stage events on the launching stream
+    stream = torch.cuda.current_stream()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+    for row in ev:
+        for e in row:
+            e.record(stream)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            layer.forward_events(S, x, out, ev[s])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    layer.check_device_error(T)
+    ms = start.elapsed_time(stop) / args.steps
+    stage_ms = np.array([[ev[s][i].elapsed_time(ev[s][i + 1]) for i in range(6)] for s in range(args.steps)]).mean(0)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = T * world / (ms / 1e3)
+
+    # ---------------- tables of the run: algorithmic bytes of FC1 (the dominant kernel)
+    off = layer.offsets(T)
+    ws = layer.ws
+    meta = ws[off["meta"]:off["meta"] + 16].view(torch.int32).cpu().numpy()
+    nne = int(meta[0])
+    counts = ws[off["counts"]:off["counts"] + 4 * (E + SHARED)].view(torch.int32).cpu().numpy()
+    routed_rows = int(counts.sum())
+    touched = int((counts > 0).sum())
+    w13_bytes_expert = 2 * I * H // 2 + 2 * I * H // 32
+    fc1_bytes = touched * w13_bytes_expert + routed_rows * (H + H // 32) + routed_rows * (I + I // 32)
+    fc1_ms = float(stage_ms[3])
+    hbm_peak, peak_kind = peaks()
+    achieved = fc1_bytes / (fc1_ms / 1e3) / 1e9
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "fc1_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            tr = json.load(f)
+        traffic = tr.get("bytes_per_launch")
+
+    # ---------------- end to end through the public API: host x/S in, host out back
+    e2e_steps = args.e2e_steps or args.steps
+    x_h = x.cpu().pin_memory()
+    S_h = S.cpu().pin_memory()
+    out_h = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xd, Sd = torch.empty_like(x), torch.empty_like(S)
+    for _ in range(2):
+        xd.copy_(x_h, non_blocking=True)
+        Sd.copy_(S_h, non_blocking=True)
+        layer.forward(Sd, xd, out)
+        out_h.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        xd.copy_(x_h, non_blocking=True)
+        Sd.copy_(S_h, non_blocking=True)
+        layer.forward(Sd, xd, out)
+        out_h.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    layer.check_device_error(T)
+
+    # ---------------- CPU baseline (rank 0, N = 1): the oracle on a bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+
+        threads = oracle.set_threads(0)
+        cb = ws[off["cta_batch"]:off["cta_batch"] + 4 * nne].view(torch.int32).cpu().numpy()
+        cl = ws[off["cta_limit"]:off["cta_limit"] + 4 * nne].view(torch.int32).cpu().numpy()
+        tb = {"cta_batch": cb, "cta_limit": cl}
+        tiles = sample_tiles_of(nne, args.cpu_tiles)
+        kg4 = H // 128
+        a13 = 2 * I * (H // 2)
+        s13 = 2 * I // 128 * kg4 * 512
+        a2 = H * (I // 2)
+        s2 = H // 128 * (I // 128) * 512
+
+        def wsrc(e):
+            return (w13[e * 2 * I:(e + 1) * 2 * I].cpu().numpy(), w13_sf[e * s13:(e + 1) * s13].cpu().numpy(),
+                    w2[e * H:(e + 1) * H].cpu().numpy(), w2_sf[e * s2:(e + 1) * s2].cpu().numpy())
+
+        qp = ws[off["q_perm"]:]
+        sfp = ws[off["sf_perm"]:]
+
+        def qsrc(c):
+            q = qp[c * 128 * H:(c + 1) * 128 * H].view(128, H).cpu().numpy()
+            sf = sfp[c * kg4 * 512:(c + 1) * kg4 * 512].cpu().numpy()
+            return q, sf
+
+        rs_bits = int(rs.view(torch.int16).item()) & 0xFFFF
+        t_topk = cpu_topk_time(S.cpu().numpy(), bias.cpu().numpy(), rs_bits)
+        t_fc = cpu_sample(tiles, tb, wsrc, qsrc, threads)
+        sec = t_topk + t_fc * nne / len(tiles)
+        cpu = {"value": T / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": (f"router top-k over all {T} rows ({t_topk:.2f} s) + oracle FC1+FC2 over {len(tiles)} of "
+                          f"{nne} token tiles ({t_fc:.2f} s), scaled by {nne}/{len(tiles)}")}
+
+    if rank == 0:
+        flops = layer_flops(T) * world
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
+            "config": {"workload": "K3-shape prefill MoE layer (config 1)", "T": T, "H": H, "I": I, "E": E, "K": K,
+                       "shared_expert_width": I, "rs": RS, "global_batch": T * world, "seq_len": T,
+                       "sequences": 16, "cu_seqlens": cu_seqlens(T).tolist(),
+                       "parallelism": f"dp{world} (experts replicated per GPU)" if world > 1 else "ep1",
+                       "l2": "inputs larger than L2: 20.96 GB of expert weights streamed every step"},
+            "tflops": flops / (ms / 1e3) / 1e12,
+            "pct_fp8_peak": flops / (ms / 1e3) / 1e12 / (FP8_PEAK_TFLOPS * world) * 100,
+            "stage_ms": dict(zip(k3moe.MoELayer.STAGES, [round(float(v), 4) for v in stage_ms])),
+            "routing": {"num_non_exiting": nne, "routed_rows": routed_rows, "touched_experts": touched},
+            "roofline": {"kernel": "FC1 grouped GEMM (grouped_gemm_kernel<0>)", "bound": "hbm",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes,
+                         "traffic": traffic},
+            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
+                    "d2h_bytes_per_step": int(out.numel() * 2)},
+            "gpu_launches": 8 * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

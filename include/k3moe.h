@@ -13,14 +13,19 @@
  *   activations x        bf16 [T, ldx]
  *   router logits S      f32  [T, lds], E_total experts wide
  *   expert weights       MXFP4: E2M1 two a byte (element 2i in the low nibble
- *                        of byte i), rows of K/2 bytes; W13 of expert e is
- *                        [gate rows 0..I-1 ; up rows I..2I-1] x H, W2 is H x I.
- *                        Experts back to back: W13 [E, 2I, H/2], W2 [E, H, I/2].
+ *                        of byte i).  W13 of expert e is [gate rows 0..I-1 ;
+ *                        up rows I..2I-1] x H, W2 is H x I, experts back to
+ *                        back (W13 [E*2I, H], W2 [E*H, I]), stored TILE-MAJOR:
+ *                        128 x 128-element tiles, tile (r/128, k/128) at index
+ *                        (r/128)*(K/128) + k/128, each tile row-major (8 KB);
+ *                        byte of element (r, k): tile*8192 + (r%128)*64 + (k%128)/2.
  *   weight scales        UE8M0 per 32 along K, 128x4-tiled over the
  *                        flattened rows (byte of row r, group kb at
- *                        ((r/128)*(K/128) + kb/4)*512 + (r%32)*16 + (r%128/32)*4 + kb%4).
- *   MXFP8 activations    E4M3 bytes [rows, K] + UE8M0 per 32 along K, in the
- *                        same tiled layout (linear [rows, K/32] where noted).
+ *                        ((r/128)*(K/128) + kb/4)*512 + (r%32)*16 + (r%128/32)*4 + kb%4):
+ *                        scale atom t belongs to data tile t.
+ *   GEMM activations     MXFP8 E4M3 in the same tile-major layout (tile*16384
+ *                        + (r%128)*128 + k%128) with scales tiled as above;
+ *                        the plain quantiser entry writes row-major q.
  *   routing tables       the reference's format (docs/k3-kernel-abi.md K14,
  *                        source/k3_moe_prefill.cu:12-35): cta_batch, cta_limit,
  *                        num_non_exiting, total_padded, route_map, exp2perm.
@@ -156,12 +161,26 @@ typedef struct k3moe_layer_args {
 
 size_t k3moe_layer_workspace_size(int T, int H, int I, int E, int K, int shared);
 int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream);
+/* The same call recording CUDA events (cudaEvent_t, may be null) on `stream`
+ * before each stage and after the last: [0] top-k, [1] tables, [2] MXFP8
+ * permute, [3] FC1, [4] FC2, [5] combine, [6] end (n_events <= 7 used). */
+int k3moe_layer_forward_events(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream,
+                               void* const* events, int n_events);
 
 /* Intermediates of the last k3moe_layer_forward inside `workspace`, for
  * inspection and tests: byte offsets of idx, wts, counts, cta_batch,
  * cta_limit, meta, route_map, exp2perm, q_perm, sf_perm, fc1_q, fc1_sf, fc2,
  * err (14 entries). */
 int k3moe_layer_workspace_offsets(int T, int H, int I, int E, int K, int shared, size_t* offsets14);
+
+/* Tracing: with a device buffer of 32 zeroed u64 set, every later FC1 / FC2
+ * launch of this process adds per-role SM cycle counters into it (FC1 at
+ * [0..15], FC2 at [16..31]): [0] producer cycles, [1] producer cycles waiting
+ * for a free stage, [2] MMA-issuer cycles, [3] waiting for a loaded stage,
+ * [4] waiting for the accumulator to be drained, [5] epilogue cycles (one
+ * warp), [6] epilogue waiting for an accumulator, [7] work units.  Summed over
+ * blocks.  Null turns tracing off (the default). */
+int k3moe_set_trace(uint64_t* counters);
 
 /* Read (and clear, when clear != 0) the two device error words at `err`:
  * returns 0 when both are zero, else K3MOE_EDEVICE with the words in out2.

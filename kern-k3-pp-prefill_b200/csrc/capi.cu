@@ -63,12 +63,14 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D K-major operand map: rows of `k` elements, a 128 x 128-element box, 128-byte swizzle.
+// Map over a tile-major operand (rows x k, both multiples of 128): viewed as
+// rows*k/128 rows of 128 elements, so one 128 x 128 box is one stored tile
+// (a contiguous 16 KB of E4M3 or 8 KB of packed E2M1); 128-byte swizzle.
 int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool fp4) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return K3MOE_EDRIVER;
-  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? k / 2 : k)};
+  const cuuint64_t dims[2] = {128, (cuuint64_t)(rows * (k / 128))};
+  const cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? 64 : 128)};
   const cuuint32_t box[2] = {128, 128};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
@@ -77,6 +79,8 @@ int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? K3MOE_OK : K3MOE_ETMAP;
 }
+
+unsigned long long* g_trace = nullptr;  // k3moe_set_trace
 
 int launch_status() { return cudaGetLastError() == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH; }
 
@@ -106,8 +110,8 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   rc = encode_operand(&tb, act, cap_rows, K, false);
   if (rc) return rc;
   GemmParams p;
-  p.sfa = w_sf;
-  p.sfb = act_sf;
+  p.sfw = w_sf;
+  p.sfa = act_sf;
   p.cta_batch = cta_batch;
   p.cta_limit = cta_limit;
   p.meta = meta;
@@ -118,10 +122,11 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   p.K = K;
   p.rows_per_expert = rows_per_expert;
   p.n_experts = n_experts;
-  p.nfb = mode == MODE_FC1 ? I / gemm::BM : H / (gemm::BM * gemm::NACC);
+  p.nfb = mode == MODE_FC1 ? I / 128 : H / gemm::BN;  // FC1: 128 features (gate + up rows), FC2: 256 outputs
   p.out_cols = mode == MODE_FC1 ? I : H;
   p.cap_rows = cap_rows;
   p.max_ctas = max_ctas;
+  p.trace = g_trace;
   const long long max_units = (long long)max_ctas * p.nfb;
   const int grid = (int)std::min<long long>(num_sms(current_device()), max_units);
   if (mode == MODE_FC1) {
@@ -278,7 +283,7 @@ int k3moe_combine(const void* fc2_bf16, const int32_t* exp2perm, const float* wt
 }
 
 int k3moe_quant_mxfp4(const float* w, long long rows, int K, uint8_t* packed, uint8_t* sf, k3moe_stream_t stream) {
-  if (rows < 0 || K <= 0 || K % 128) return K3MOE_EINVAL;
+  if (rows < 0 || rows % 128 || K <= 0 || K % 128) return K3MOE_EINVAL;
   if (rows == 0) return K3MOE_OK;
   const long long groups = rows * (K / 32);
   const int grid = (int)std::min<long long>(cdiv(groups, 256), (long long)num_sms(current_device()) * 32);
@@ -288,7 +293,7 @@ int k3moe_quant_mxfp4(const float* w, long long rows, int K, uint8_t* packed, ui
 
 int k3moe_synth_mxfp4(uint64_t seed, long long row0, long long rows, int K, float sd, uint8_t* packed, uint8_t* sf,
                       k3moe_stream_t stream) {
-  if (rows < 0 || row0 < 0 || K <= 0 || K % 128 || row0 % 128) return K3MOE_EINVAL;
+  if (rows < 0 || rows % 128 || row0 < 0 || K <= 0 || K % 128 || row0 % 128) return K3MOE_EINVAL;
   if (rows == 0) return K3MOE_OK;
   const long long groups = rows * (K / 32);
   const int grid = (int)std::min<long long>(cdiv(groups, 256), (long long)num_sms(current_device()) * 32);
@@ -309,8 +314,9 @@ int k3moe_layer_workspace_offsets(int T, int H, int I, int E, int K, int shared,
   return K3MOE_OK;
 }
 
-int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream) {
-  if (!a || !workspace) return K3MOE_EINVAL;
+int k3moe_layer_forward_events(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream,
+                               void* const* events, int n_events) {
+  if (!a || !workspace || (n_events > 0 && !events)) return K3MOE_EINVAL;
   const int shared = a->shared ? 1 : 0;
   if (a->T < 1 || a->H % 256 || a->I % 256 || a->E < a->K || a->E > 1024 || a->ldx < a->H || a->ldo < a->H)
     return K3MOE_EINVAL;
@@ -320,26 +326,46 @@ int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_by
   auto I32 = [&](int i) { return reinterpret_cast<int32_t*>(ws + L.off[i]); };
   auto U8 = [&](int i) { return reinterpret_cast<uint8_t*>(ws + L.off[i]); };
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto mark = [&](int i) {
+    if (i < n_events && events[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(events[i]), s);
+  };
   uint32_t* err = reinterpret_cast<uint32_t*>(ws + L.off[L_ERR]);
   if (cudaMemsetAsync(err, 0, 8, s) != cudaSuccess) return K3MOE_ELAUNCH;
   float* wts = reinterpret_cast<float*>(ws + L.off[L_WTS]);
+  mark(0);
   int rc = k3moe_route_topk(a->S, a->lds, a->bias, a->rs, a->T, a->E, a->K, I32(L_IDX), wts, stream);
   if (rc) return rc;
+  mark(1);
   // the route scratch (block counts / offsets) sits at the end of the layout
   rc = k3moe_route_tables(I32(L_IDX), a->T, a->K, 0, a->E, shared, 128, ws + L.blockcount, I32(L_COUNTS),
                           I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META), I32(L_ROUTE_MAP), I32(L_EXP2PERM), stream);
   if (rc) return rc;
+  mark(2);
   rc = k3moe_quant_permute(a->x, a->ldx, a->T, a->H, a->K, I32(L_EXP2PERM), I32(L_META), U8(L_QP), U8(L_SFP), stream);
   if (rc) return rc;
+  mark(3);
   const int nexp = a->E + shared;
   rc = k3moe_fc1(a->w13, a->w13_sf, U8(L_QP), U8(L_SFP), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META), U8(L_FC1Q),
                  U8(L_FC1SF), a->H, a->I, nexp, L.cap_rows, L.max_ctas, err, stream);
   if (rc) return rc;
+  mark(4);
   rc = k3moe_fc2(a->w2, a->w2_sf, U8(L_FC1Q), U8(L_FC1SF), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META),
                  ws + L.off[L_FC2], a->H, a->I, nexp, L.cap_rows, L.max_ctas, err, stream);
   if (rc) return rc;
-  return k3moe_combine(ws + L.off[L_FC2], I32(L_EXP2PERM), wts, I32(L_META), a->out, a->ldo, a->T, a->T, a->K, a->H,
-                       stream);
+  mark(5);
+  rc = k3moe_combine(ws + L.off[L_FC2], I32(L_EXP2PERM), wts, I32(L_META), a->out, a->ldo, a->T, a->T, a->K, a->H,
+                     stream);
+  mark(6);
+  return rc;
+}
+
+int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream) {
+  return k3moe_layer_forward_events(a, workspace, ws_bytes, stream, nullptr, 0);
+}
+
+int k3moe_set_trace(uint64_t* counters) {
+  g_trace = reinterpret_cast<unsigned long long*>(counters);
+  return K3MOE_OK;
 }
 
 int k3moe_read_error(uint32_t* err, uint32_t* out2, int clear, k3moe_stream_t stream) {

@@ -64,6 +64,24 @@ __device__ __forceinline__ int mx8_exponent(float amax) {
   return min(max(e, -127), 127);
 }
 
+// The same exponent by exact arithmetic on the f32 quotient q = amax / 448
+// (IEEE division): the exponent of q, plus one unless q is a power of two.
+// Used where no reference rounding chain must be mirrored (FC1's output).
+__device__ __forceinline__ int mx8_exponent_exact(float amax) {
+  if (!(amax > 0.f)) return 0;
+  const u32 b = __float_as_uint(__fdiv_rn(amax, 448.f));
+  int e;
+  if ((b >> 23) != 0) {
+    e = (int)(b >> 23) - 127 + ((b & 0x7fffffu) ? 1 : 0);
+  } else {  // subnormal quotient: below 2^-126, clamped anyway
+    e = -127;
+  }
+  return min(max(e, -127), 127);
+}
+
+// 2^n as an f32 built from its bits, n in [-126, 127]
+__device__ __forceinline__ float pow2_normal(int n) { return __uint_as_float((u32)(n + 127) << 23); }
+
 // bf16 pairs as bits: a bf16 is the top half of its f32.
 __device__ __forceinline__ float2 bf16x2_to_f2(u32 u) {
   return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
@@ -81,6 +99,19 @@ __device__ __forceinline__ u32 f2_to_bf16x2(float lo, float hi) {
 // the tensor-core scale copy (tcgen05.cp 32x128b.warpx4) reads atom by atom.
 __host__ __device__ __forceinline__ long long sf_tiled_offset(long long r, int kb, int kgroups4) {
   return ((r >> 7) * kgroups4 + (kb >> 2)) * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + (kb & 3);
+}
+
+// Tile-major operand layout of the grouped GEMMs: a [rows, K] matrix (rows and
+// K multiples of 128) is stored as 128 x 128-element tiles, tile (r/128, k/128)
+// at index (r/128) * (K/128) + k/128, each tile row-major.  One pipeline
+// stage's TMA box is then one contiguous chunk (16 KB of E4M3, 8 KB of packed
+// E2M1), and the tile index equals the index of its 512-byte scale atom.
+__host__ __device__ __forceinline__ long long op8_offset(long long r, int k, int K) {
+  return (((r >> 7) * (K >> 7) + (k >> 7)) << 14) + ((r & 127) << 7) + (k & 127);
+}
+// packed E2M1 (two elements a byte, element 2i in the low nibble of byte i): byte of element k
+__host__ __device__ __forceinline__ long long op4_offset(long long r, int k, int K) {
+  return (((r >> 7) * (K >> 7) + (k >> 7)) << 13) + ((r & 127) << 6) + ((k & 127) >> 1);
 }
 
 // ---------------------------------------------------------------- shared memory / mbarrier
@@ -140,6 +171,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, u32 bytes,
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+// bring a tensor-map box into L2 (no shared memory, no completion to wait on)
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(c0), "r"(c1)
+               : "memory");
+}
+// bring `bytes` (a multiple of 16, 16-byte aligned) into L2
+__device__ __forceinline__ void bulk_prefetch(const void* src, u32 bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
@@ -217,13 +257,15 @@ __device__ __forceinline__ u64 sdesc_sf(u32 saddr) {
 }
 
 // Instruction descriptor of kind::mxf8f6f4 with UE8M0 scales, K-major A and B,
-// A = E2M1 (weights), B = E4M3 (activations), M = 128, N = n (multiple of 8).
+// M = 128, N = n (multiple of 8, <= 256).  Formats: 0 = E4M3, 5 = E2M1.
 // The scale-factor ids select the byte of the scale column (the K block).
-__device__ __forceinline__ u32 idesc_mxf8f6f4(int n, u32 a_sf_id, u32 b_sf_id) {
+enum : u32 { FMT_E4M3 = 0, FMT_E2M1 = 5 };
+__device__ __forceinline__ u32 idesc_mxf8f6f4(int n, u32 a_sf_id, u32 b_sf_id, u32 a_fmt = FMT_E2M1,
+                                              u32 b_fmt = FMT_E4M3) {
   u32 d = 0;
   d |= (b_sf_id & 3u) << 4;
-  d |= 5u << 7;                  // A format E2M1
-  d |= 0u << 10;                 // B format E4M3
+  d |= a_fmt << 7;               // A format
+  d |= b_fmt << 10;              // B format
   d |= (u32)(n >> 3) << 17;      // N >> 3
   d |= 1u << 23;                 // scale type UE8M0
   d |= (128u >> 4) << 24;        // M >> 4

@@ -1,71 +1,82 @@
 // Grouped (per-expert) block-scaled GEMMs of the routed MoE on 5th-gen tensor
-// cores: FC1 = [gate; up] x act -> SwiGLU -> MXFP8 (E4M3 + UE8M0 per 32), and
-// FC2 = down x act1 -> bf16.  They replace the two TRT-LLM-gen batched-GEMM
-// cubins of the reference (kernels.toml:1-9; op arguments
+// cores: FC1 = act x [gate; up]^T -> SwiGLU -> MXFP8 (E4M3 + UE8M0 per 32),
+// and FC2 = act1 x down^T -> bf16.  They replace the two TRT-LLM-gen
+// batched-GEMM cubins of the reference (kernels.toml:1-9; op arguments
 // scripts/k3_moe_bmm.py:131-134, 167-169; contract docs/k3-kernel-abi.md:535-565).
 //
-// Operands.  A = expert weights, MXFP4 (E2M1 packed two a byte, UE8M0 per 32
-// along K), loaded by TMA with the 16U4_ALIGN16B type that unpacks them into
-// the byte-per-element shared-memory form kind::mxf8f6f4 reads.  B = the
-// activations, MXFP8 rows in permuted (expert-grouped) order.  The weight is
-// the MMA's M side (128 rows an accumulator) and the tokens its N side, so a
-// tile of n routed rows issues N = roundup(n, 8) columns, not a padded 128.
+// Operands.  A = the activations: 128 permuted token rows of MXFP8 (one
+// routing tile).  B = 256 rows of expert weights, MXFP4 (E2M1 packed two a
+// byte, UE8M0 per 32 along K), loaded by TMA with the 16U4_ALIGN16B type that
+// unpacks them into the byte-per-element form kind::mxf8f6f4 reads.  One MMA
+// is M=128 x N=256 x K=32: the full-rate shape (an M=128 MMA costs the same
+// ~75 cycles for any N <= 128, so weight rows are put on the N side, 256 at a
+// time, and the tokens of a tile on M).  FC1's 256 weight rows are the gate
+// and the up rows of the same 128 features, so every accumulator row holds a
+// token's gate and up values side by side.
 //
 // Tiles.  The routing tables (cta_batch / cta_limit / num_non_exiting, the
-// reference's format) cut every expert's rows into 128-row token tiles; a
-// work unit is (token tile c, feature block fb).  FC1's unit holds the gate
-// and the up accumulator of 128 features (two M=128 accumulators); FC2's holds
-// 256 output features.  A persistent grid walks the units round-robin.
+// reference's format) cut every expert's rows into 128-row token tiles; a work
+// unit is (token tile c, 256-row weight block fb).  A persistent grid walks
+// the units round-robin, so the weight blocks of one tile run side by side
+// and its activation tile is read from L2.
 //
-// Roles (192 threads): warp 0 lane 0 issues TMA (operands) and bulk copies
+// Roles (320 threads): warp 0 lane 0 issues TMA (operands) and bulk copies
 // (scale atoms); warp 1 lane 0 copies the scale atoms into tensor memory
-// (tcgen05.cp) and issues the MMAs; warps 2-5 are the epilogue, each reading
-// its 32-lane sub-partition of the accumulators.  A 4-stage mbarrier ring
-// carries K blocks of 128; every wait is bounded and reports instead of
-// hanging.
+// (tcgen05.cp) and issues the MMAs; warps 2-9 are the epilogue.  An epilogue
+// warp reads its sub-partition's 32 token rows and one half of the columns
+// into registers, releases the accumulator, and only then computes and
+// stores, so the next unit's MMAs overlap the math and the stores.  A 4-stage
+// mbarrier ring carries K blocks of 128; every wait is bounded and reports
+// instead of hanging.
 #include "common.cuh"
 
 namespace k3 {
 
 namespace gemm {
-constexpr int BM = 128;                  // weight rows an accumulator
-constexpr int BN = 128;                  // token rows a tile (the routing tile)
+constexpr int BM = 128;                  // token rows a tile (the routing tile): the MMA's M
+constexpr int BN = 256;                  // weight rows a unit: the MMA's N
 constexpr int BK = 128;                  // K elements a stage
-constexpr int NACC = 2;                  // accumulators a tile
 constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK;         // unpacked E2M1: a byte an element in shared memory
-constexpr int B_BYTES = BN * BK;
+#ifndef K3MOE_PREFETCH
+#define K3MOE_PREFETCH 0
+#endif
+constexpr int PREFETCH = K3MOE_PREFETCH;  // k-stages an L2 prefetch runs ahead of the loads (0: none)
+constexpr int A_BYTES = BM * BK;         // activation tile (E4M3)
+constexpr int W_TILE = 128 * BK;         // one 128-row weight tile, unpacked E2M1 (a byte an element)
+constexpr int B_BYTES = 2 * W_TILE;
 constexpr int SF_BYTES = 512;            // one 128-row x 4-group scale atom
-constexpr int OPS_STAGE = NACC * A_BYTES + B_BYTES;          // 48 KB, 1024-aligned
-constexpr int SF_STAGE = (NACC + 1) * SF_BYTES;               // 1.5 KB
+constexpr int OPS_STAGE = A_BYTES + B_BYTES;                  // 48 KB, 1024-aligned
+constexpr int SF_STAGE = 3 * SF_BYTES;                        // activation atom + two weight atoms
 // bytes a stage's copies complete on its barrier: a 16U4_ALIGN16B load counts
 // the packed (global) bytes, half the unpacked tile it writes
-constexpr u32 STAGE_TX = NACC * A_BYTES / 2 + B_BYTES + SF_STAGE;
+constexpr u32 STAGE_TX = A_BYTES + B_BYTES / 2 + SF_STAGE;
 constexpr int SMEM_BYTES = STAGES * (OPS_STAGE + SF_STAGE) + 1024 /*align*/ + 256 /*barriers*/;
 constexpr u32 TMEM_COLS = 512;
-constexpr int SF_TMEM_COL = NACC * BN;   // scale columns after the accumulators
-constexpr int THREADS = 192;
+constexpr int SF_TMEM_COL = BN;          // scale columns after the accumulator
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
 }  // namespace gemm
 
 enum { MODE_FC1 = 0, MODE_FC2 = 1 };
 
 struct GemmParams {
-  const uint8_t* sfa;       // weight scales, tiled over all weight rows, K/128 atoms a row block
-  const uint8_t* sfb;       // activation scales, tiled over permuted rows
+  const uint8_t* sfw;       // weight scales, tiled over all weight rows (atom t of data tile t)
+  const uint8_t* sfa;       // activation scales, tiled over permuted rows
   const int* cta_batch;     // [ctas] local expert of token tile c
   const int* cta_limit;     // [ctas] end of tile c's real rows
   const int* meta;          // meta[0] = num_non_exiting
-  uint8_t* out_q;           // FC1: [cap_rows, out_cols] E4M3
+  uint8_t* out_q;           // FC1: [cap_rows, out_cols] E4M3, tile-major
   uint8_t* out_sf;          // FC1: tiled scales over permuted rows
-  bf16* out_bf16;           // FC2: [cap_rows, out_cols]
+  bf16* out_bf16;           // FC2: [cap_rows, out_cols] row-major
   u32* err;
   int K;                    // reduction length (elements), multiple of 128
   int rows_per_expert;      // weight rows an expert: FC1 2I, FC2 H
   int n_experts;            // experts the weight tensor holds
-  int nfb;                  // feature blocks a token tile
+  int nfb;                  // weight blocks a token tile: FC1 I/128, FC2 H/256
   int out_cols;             // FC1 I, FC2 H
-  int cap_rows;             // permuted-row capacity of B and the outputs
+  int cap_rows;             // permuted-row capacity of the activations and the outputs
   int max_ctas;             // capacity of the CTA tables
+  unsigned long long* trace;  // optional per-role cycle counters (16 a mode), or null
 };
 
 struct Unit {
@@ -77,29 +88,30 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u) {
   const int c = u / p.nfb;
   w.fb = u % p.nfb;
   w.e = p.cta_batch[c];
-  w.row0 = c * gemm::BN;
+  w.row0 = c * gemm::BM;
   w.n = p.cta_limit[c] - w.row0;
-  w.valid = c < p.max_ctas && w.e >= 0 && w.e < p.n_experts && w.n > 0 && w.n <= gemm::BN &&
-            w.row0 + gemm::BN <= p.cap_rows;
+  w.valid = c < p.max_ctas && w.e >= 0 && w.e < p.n_experts && w.n > 0 && w.n <= gemm::BM &&
+            w.row0 + gemm::BM <= p.cap_rows;
   return w;
 }
 
-// weight row of accumulator a of unit w
+// first weight row of the h-th 128-row half of unit w's weight block:
+// FC1 pairs the gate rows of features [128 fb, 128 fb + 128) with their up rows
 template <int MODE>
-__device__ __forceinline__ int weight_row(const GemmParams& p, const Unit& w, int a) {
-  if (MODE == MODE_FC1) return w.e * p.rows_per_expert + a * (p.rows_per_expert / 2) + w.fb * gemm::BM;
-  return w.e * p.rows_per_expert + (w.fb * gemm::NACC + a) * gemm::BM;
+__device__ __forceinline__ int weight_row(const GemmParams& p, const Unit& w, int h) {
+  if (MODE == MODE_FC1) return w.e * p.rows_per_expert + h * (p.rows_per_expert / 2) + w.fb * 128;
+  return w.e * p.rows_per_expert + w.fb * gemm::BN + h * 128;
 }
 
 template <int MODE>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                         GemmParams p) {
   using namespace gemm;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ops = smem;                                  // [STAGES][A0 | A1 | B]
-  uint8_t* sfs = smem + STAGES * OPS_STAGE;             // [STAGES][SFA0 | SFA1 | SFB]
+  uint8_t* ops = smem;                                  // [STAGES][A | W0 | W1]
+  uint8_t* sfs = smem + STAGES * OPS_STAGE;             // [STAGES][SFA | SFW0 | SFW1]
   u64* bars = reinterpret_cast<u64*>(sfs + STAGES * SF_STAGE);
   u64* full = bars;                                     // [STAGES]
   u64* empty = bars + STAGES;                           // [STAGES]
@@ -120,12 +132,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty, EPI_WARPS);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    prefetch_tmap(&tmW);
     prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
   }
   tc_fence_before();
   __syncthreads();
@@ -142,30 +154,60 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       int stage = 0;
       u32 phase = 0;
       int armed[STAGES] = {0, 0, 0, 0};
+      const long long t_role = clock64();
+      long long t_wait = 0;
+      // optional L2 prefetch cursor PREFETCH stages ahead of the shared-memory loads
+      int pu = blockIdx.x, pks = 0;
+      Unit pw = {};
+      if (PREFETCH > 0 && pu < units) pw = decode_unit(p, pu);
+      auto prefetch_next = [&]() {
+        while (pu < units && !pw.valid) {
+          pu += gridDim.x;
+          if (pu < units) pw = decode_unit(p, pu);
+        }
+        if (pu >= units) return;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int t = (weight_row<MODE>(p, pw, h) / 128) * kstages + pks;
+          tma_prefetch_2d(&tmW, 0, t * 128);
+          bulk_prefetch(p.sfw + (long long)t * SF_BYTES, SF_BYTES);
+        }
+        if (++pks == kstages) {
+          pks = 0;
+          pu += gridDim.x;
+          if (pu < units) pw = decode_unit(p, pu);
+        }
+      };
+      for (int i = 0; i < PREFETCH; ++i) prefetch_next();
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         const Unit w = decode_unit(p, u);
         if (!w.valid) {
           report_error(p.err, ERR_BAD_TABLE, 0x100u + MODE);
           continue;
         }
-        int arow[NACC];
-#pragma unroll
-        for (int a = 0; a < NACC; ++a) arow[a] = weight_row<MODE>(p, w, a);
+        int wrow[2];
+        wrow[0] = weight_row<MODE>(p, w, 0);
+        wrow[1] = weight_row<MODE>(p, w, 1);
         for (int ks = 0; ks < kstages; ++ks) {
+          if (PREFETCH > 0) prefetch_next();
+          const long long t0 = clock64();
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, 0x200u + MODE)) break;
+          t_wait += clock64() - t0;
           uint8_t* st = ops + stage * OPS_STAGE;
           uint8_t* sf = sfs + stage * SF_STAGE;
           mbar_arrive_expect_tx(&full[stage], STAGE_TX);
           ++armed[stage];
+          // tile-major operands: tile t = row_block * kstages + ks is rows [128 t, 128 t + 128) of the
+          // maps (one contiguous chunk), and its scales are the 512-byte atom t
+          const int ta = (w.row0 / BM) * kstages + ks;
+          tma_load_2d(st, &tmA, &full[stage], 0, ta * BM);
+          bulk_load(sf, p.sfa + (long long)ta * SF_BYTES, SF_BYTES, &full[stage]);
 #pragma unroll
-          for (int a = 0; a < NACC; ++a) {
-            tma_load_2d(st + a * A_BYTES, &tmA, &full[stage], ks * BK, arow[a]);
-            bulk_load(sf + a * SF_BYTES, p.sfa + ((long long)(arow[a] / BM) * kstages + ks) * SF_BYTES, SF_BYTES,
-                      &full[stage]);
+          for (int h = 0; h < 2; ++h) {
+            const int t = (wrow[h] / 128) * kstages + ks;
+            tma_load_2d(st + A_BYTES + h * W_TILE, &tmW, &full[stage], 0, t * 128);
+            bulk_load(sf + (1 + h) * SF_BYTES, p.sfw + (long long)t * SF_BYTES, SF_BYTES, &full[stage]);
           }
-          tma_load_2d(st + NACC * A_BYTES, &tmB, &full[stage], ks * BK, w.row0);
-          bulk_load(sf + NACC * SF_BYTES, p.sfb + ((long long)(w.row0 / BN) * kstages + ks) * SF_BYTES, SF_BYTES,
-                    &full[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -175,6 +217,10 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       // every armed stage's last fill has landed before the block may exit
       for (int s = 0; s < STAGES; ++s)
         if (armed[s]) mbar_wait(&full[s], (u32)(armed[s] - 1) & 1u, nullptr, p.err, 0x300u + MODE, 100000000ull);
+      if (p.trace) {
+        atomicAdd(p.trace + MODE * 16 + 0, (unsigned long long)(clock64() - t_role));
+        atomicAdd(p.trace + MODE * 16 + 1, (unsigned long long)t_wait);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -182,34 +228,38 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       int stage = 0;
       u32 phase = 0, acc_phase = 0;
       bool issued = false;
+      const long long t_role = clock64();
+      long long t_wfull = 0, t_wacc = 0, n_units = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         const Unit w = decode_unit(p, u);
         if (!w.valid) continue;
-        const int N = (w.n + 7) & ~7;
+        long long t0 = clock64();
         if (!mbar_wait(acc_empty, acc_phase ^ 1u, abort_flag, p.err, 0x400u + MODE)) break;
+        t_wacc += clock64() - t0;
+        ++n_units;
         tc_fence_after();
         bool ok = true;
         for (int ks = 0; ks < kstages; ++ks) {
+          t0 = clock64();
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, 0x500u + MODE)) {
             ok = false;
             break;
           }
+          t_wfull += clock64() - t0;
           tc_fence_after();
           const u32 st = smem_u32(ops + stage * OPS_STAGE);
           const u32 sf = smem_u32(sfs + stage * SF_STAGE);
           const u32 sf_col = tmem_base + SF_TMEM_COL + stage * 16;
+          // scale columns: [0,4) the activation atom, [4,8) and [8,12) the two weight atoms
 #pragma unroll
-          for (int a = 0; a <= NACC; ++a) tmem_cp_32x128b_x4(sf_col + 4 * a, sdesc_sf(sf + a * SF_BYTES));
+          for (int q = 0; q < 3; ++q) tmem_cp_32x128b_x4(sf_col + 4 * q, sdesc_sf(sf + q * SF_BYTES));
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
-            const u32 idesc = idesc_mxf8f6f4(N, (u32)kk, (u32)kk);
-            const u64 bdesc = sdesc_k_sw128(st + NACC * A_BYTES + kk * 32);
-#pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-              const u64 adesc = sdesc_k_sw128(st + a * A_BYTES + kk * 32);
-              mma_mxf8f6f4(tmem_base + a * BN, adesc, bdesc, idesc, (sf_col + 4 * a) | ((u32)kk << 30),
-                           (sf_col + 4 * NACC) | ((u32)kk << 30), (ks | kk) != 0);
-            }
+            const u32 idesc = idesc_mxf8f6f4(BN, (u32)kk, (u32)kk, FMT_E4M3, FMT_E2M1);
+            const u64 adesc = sdesc_k_sw128(st + kk * 32);
+            const u64 bdesc = sdesc_k_sw128(st + A_BYTES + kk * 32);
+            mma_mxf8f6f4(tmem_base, adesc, bdesc, idesc, sf_col | ((u32)kk << 30), (sf_col + 4) | ((u32)kk << 30),
+                         (ks | kk) != 0);
           }
           tc_commit(&empty[stage]);
           issued = true;
@@ -227,62 +277,101 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         tc_commit(drain);
         mbar_wait(drain, 0, nullptr, p.err, 0x600u + MODE, 100000000ull);
       }
+      if (p.trace) {
+        atomicAdd(p.trace + MODE * 16 + 2, (unsigned long long)(clock64() - t_role));
+        atomicAdd(p.trace + MODE * 16 + 3, (unsigned long long)t_wfull);
+        atomicAdd(p.trace + MODE * 16 + 4, (unsigned long long)t_wacc);
+        atomicAdd(p.trace + MODE * 16 + 7, (unsigned long long)n_units);
+      }
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5)
-    const int sub = warp & 3;                 // tensor-memory sub-partition of this warp
+    // ------------------------------------------------ epilogue (warps 2..9)
+    // warp -> (sub-partition, column half): its thread i owns token row 32*sub + i of the tile
+    const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;
     const u32 lane_base = (u32)(sub * 32) << 16;
+    const int row = sub * 32 + lane;
     u32 acc_phase = 0;
+    const long long t_role = clock64();
+    long long t_wait = 0;
     for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
       const Unit w = decode_unit(p, u);
       if (!w.valid) continue;
+      const long long t0 = clock64();
       if (!mbar_wait(acc_full, acc_phase, abort_flag, p.err, 0x700u + MODE)) break;
+      t_wait += clock64() - t0;
       tc_fence_after();
+      u32 v[4][32];
       if (MODE == MODE_FC1) {
-        const int f = w.fb * BM + sub * 32 + lane;  // this lane's feature
-        const int kb = (w.fb * BM + sub * 32) / 32;
-        const int kg4 = p.out_cols / 128;
-        for (int j0 = 0; j0 < w.n; j0 += 32) {
-          u32 g[32], v[32];
-          tmem_ld32(tmem_base + lane_base + (u32)j0, g);
-          tmem_ld32(tmem_base + lane_base + (u32)(BN + j0), v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            if (j0 + jj < w.n) {
-              const float gf = __uint_as_float(g[jj]);
-              const float uf = __uint_as_float(v[jj]);
-              const float h = gf / (1.0f + __expf(-gf)) * uf;
-              const u32 am = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h)));
-              const int e = mx8_exponent(__uint_as_float(am));
-              const float s = exp2f((float)-e);
-              const long long r = w.row0 + j0 + jj;
-              p.out_q[r * p.out_cols + f] = (uint8_t)(e4m3x2_sat(h * s, 0.f) & 0xffu);
-              if (lane == 0) p.out_sf[sf_tiled_offset(r, kb, kg4)] = (uint8_t)(e + 127);
-            }
-          }
-        }
+        // gate of features [64 half, 64 half + 64) in columns 64 half.., their up 128 columns later
+        const u32 c0 = (u32)(64 * half);
+        tmem_ld32(tmem_base + lane_base + c0, v[0]);
+        tmem_ld32(tmem_base + lane_base + c0 + 32, v[1]);
+        tmem_ld32(tmem_base + lane_base + c0 + 128, v[2]);
+        tmem_ld32(tmem_base + lane_base + c0 + 160, v[3]);
       } else {
-        for (int a = 0; a < NACC; ++a) {
-          const int f = (w.fb * NACC + a) * BM + sub * 32 + lane;
-          for (int j0 = 0; j0 < w.n; j0 += 32) {
-            u32 v[32];
-            tmem_ld32(tmem_base + lane_base + (u32)(a * BN + j0), v);
-            tmem_wait_ld();
+        const u32 c0 = (u32)(128 * half);
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) {
-              if (j0 + jj < w.n) {
-                const long long r = w.row0 + j0 + jj;
-                p.out_bf16[r * p.out_cols + f] = __float2bfloat16_rn(__uint_as_float(v[jj]));
-              }
-            }
-          }
-        }
+        for (int q = 0; q < 4; ++q) tmem_ld32(tmem_base + lane_base + c0 + 32 * q, v[q]);
       }
+      tmem_wait_ld();
+      // the accumulator is in registers: release it to the next unit's MMAs
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       acc_phase ^= 1u;
+      if (row < w.n) {
+        const long long r = w.row0 + row;
+        if (MODE == MODE_FC1) {
+          const int kg4 = p.out_cols / 128;
+          u32 sfw = 0;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            float hv[32];
+            float amax = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float gf = __uint_as_float(v[g][j]);
+              const float uf = __uint_as_float(v[2 + g][j]);
+              hv[j] = __fdividef(gf, 1.0f + __expf(-gf)) * uf;
+              amax = fmaxf(amax, fabsf(hv[j]));
+            }
+            const int e = mx8_exponent_exact(amax);
+            const float s = pow2_normal(-e);
+            u32 q[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              q[j] = (u32)e4m3x2_sat(hv[4 * j] * s, hv[4 * j + 1] * s) |
+                     ((u32)e4m3x2_sat(hv[4 * j + 2] * s, hv[4 * j + 3] * s) << 16);
+            const int f = w.fb * 128 + 64 * half + 32 * g;
+            uint4* dst = reinterpret_cast<uint4*>(p.out_q + op8_offset(r, f, p.out_cols));
+            dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
+            dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+            sfw |= (u32)(e + 127) << (8 * g);
+          }
+          // the two groups' scales are adjacent bytes of one atom row (kb even)
+          const int kb = (w.fb * 128 + 64 * half) / 32;
+          *reinterpret_cast<unsigned short*>(p.out_sf + sf_tiled_offset(r, kb, kg4)) = (unsigned short)sfw;
+        } else {
+          bf16* dst = p.out_bf16 + r * p.out_cols + w.fb * BN + 128 * half;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 o;
+              o.x = f2_to_bf16x2(__uint_as_float(v[q][j]), __uint_as_float(v[q][j + 1]));
+              o.y = f2_to_bf16x2(__uint_as_float(v[q][j + 2]), __uint_as_float(v[q][j + 3]));
+              o.z = f2_to_bf16x2(__uint_as_float(v[q][j + 4]), __uint_as_float(v[q][j + 5]));
+              o.w = f2_to_bf16x2(__uint_as_float(v[q][j + 6]), __uint_as_float(v[q][j + 7]));
+              *reinterpret_cast<uint4*>(dst + 32 * q + j) = o;
+            }
+          }
+        }
+      }
+    }
+    if (p.trace && lane == 0 && warp == 2) {
+      atomicAdd(p.trace + MODE * 16 + 5, (unsigned long long)(clock64() - t_role));
+      atomicAdd(p.trace + MODE * 16 + 6, (unsigned long long)t_wait);
     }
   }
   tc_fence_before();

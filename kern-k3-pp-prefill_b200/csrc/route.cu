@@ -246,7 +246,8 @@ __device__ __forceinline__ uint2 quant8_lanes(const uint4 u, int& sfbyte) {
 
 // Quantise rows of x (row stride ldx elements, `cols` a multiple of 256) and
 // write q/sf to every permuted row the row is routed to (exp2perm, plus the
-// shared expert's row).  SF in the 128x4-tiled layout over permuted rows.
+// shared expert's row).  q in the tile-major operand layout (op8_offset), SF in
+// the 128x4-tiled layout over permuted rows.
 // One warp a row; a lane covers 8 columns of each 256-column piece.
 __global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restrict__ x, int ldx, int R, int cols, int K,
                                                             const int* __restrict__ exp2perm,
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restri
       sfw |= __shfl_down_sync(0xffffffffu, sfw, 8);
       for (int d = 0; d < nd; ++d) {
         const long long p = dst[d];
-        *reinterpret_cast<uint2*>(qp + p * cols + c) = w;
+        *reinterpret_cast<uint2*>(qp + op8_offset(p, c, cols)) = w;
         if ((lane & 15) == 0) *reinterpret_cast<u32*>(sfp + sf_tiled_offset(p, kb, kg4)) = sfw;
       }
     }
@@ -431,10 +432,10 @@ __host__ __device__ __forceinline__ int mx4_exponent(float amax) {
   return x < -127 ? -127 : (x > 127 ? 127 : x);
 }
 
-// w f32 [rows, K] -> packed [rows, K/2] (element 2i in the low nibble of byte i)
-// and scales in the 128x4-tiled layout per `sf_rows_per_block` row block:
-// the scale of (row r, group kb) is at sf_tiled_offset(r, kb, ceil(K/128)).
-// One thread a 32-element group.
+// w f32 [rows, K] -> packed E2M1 (element 2i in the low nibble of byte i) in
+// the tile-major operand layout (op4_offset; rows a multiple of 128) and
+// scales in the 128x4-tiled layout: the scale of (row r, group kb) is at
+// sf_tiled_offset(r, kb, K/128).  One thread a 32-element group.
 __global__ void __launch_bounds__(256) quant_mxfp4_kernel(const float* __restrict__ w, long long rows, int K,
                                                           uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
   const int kbn = K / 32, kg4 = (kbn + 3) / 4;
@@ -456,7 +457,7 @@ __global__ void __launch_bounds__(256) quant_mxfp4_kernel(const float* __restric
     u32 out[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int j = 0; j < 32; ++j) out[j >> 3] |= e2m1_code(v[j] * inv) << (4 * (j & 7));
-    uint4* dst = reinterpret_cast<uint4*>(packed + r * (K / 2) + kb * 16);
+    uint4* dst = reinterpret_cast<uint4*>(packed + op4_offset(r, kb * 32, K));
     *dst = make_uint4(out[0], out[1], out[2], out[3]);
     sf[sf_tiled_offset(r, kb, kg4)] = (uint8_t)(x + 127);
   }
@@ -502,7 +503,7 @@ __global__ void __launch_bounds__(256) synth_mxfp4_kernel(u64 seed, long long ro
     u32 out[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int j = 0; j < 32; ++j) out[j >> 3] |= e2m1_code(v[j] * inv) << (4 * (j & 7));
-    *reinterpret_cast<uint4*>(packed + r * (K / 2) + kb * 16) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(packed + op4_offset(r, kb * 32, K)) = make_uint4(out[0], out[1], out[2], out[3]);
     sf[sf_tiled_offset(r, kb, kg4)] = (uint8_t)(x + 127);
   }
 }

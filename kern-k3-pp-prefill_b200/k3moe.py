@@ -45,9 +45,19 @@ SIGNATURES = {
     "k3moe_synth_mxfp4": (_I, [_U64, _L, _L, _I, _F, _P, _P, _P]),
     "k3moe_layer_workspace_size": (_SZ, [_I, _I, _I, _I, _I, _I]),
     "k3moe_layer_forward": (_I, [_P, _P, _SZ, _P]),
+    "k3moe_layer_forward_events": (_I, [_P, _P, _SZ, _P, _P, _I]),
     "k3moe_layer_workspace_offsets": (_I, [_I, _I, _I, _I, _I, _I, _P]),
     "k3moe_read_error": (_I, [_P, _P, _I, _P]),
+    "k3moe_set_trace": (_I, [_P]),
 }
+
+TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",
+                "epilogue_wait_acc", "units"]
+
+
+def set_trace(buf):
+    """Enable GEMM role counters into a zeroed uint64 device tensor of 32 entries (None disables)."""
+    _check(lib().k3moe_set_trace(_p(buf)), "set_trace")
 
 
 class K3MoeError(RuntimeError):
@@ -264,6 +274,17 @@ class MoELayer:
         a = self.args(S, x, out, T)
         _check(lib().k3moe_layer_forward(ctypes.byref(a), self.ws.data_ptr(), self.ws_bytes, _stream(stream)),
                "layer_forward")
+        return out
+
+    STAGES = ["topk", "tables", "permute", "fc1", "fc2", "combine"]
+
+    def forward_events(self, S, x, out, events, stream=None):
+        """forward() recording torch.cuda.Event objects before each stage and after the last (7 events)."""
+        T = x.shape[0]
+        a = self.args(S, x, out, T)
+        arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+        _check(lib().k3moe_layer_forward_events(ctypes.byref(a), self.ws.data_ptr(), self.ws_bytes, _stream(stream),
+                                                ctypes.cast(arr, ctypes.c_void_p), len(events)), "layer_forward")
         return out
 
     def offsets(self, T=None):

@@ -26,6 +26,11 @@ float orc_e4m3_to_f32(uint8_t b);
 float orc_e2m1_to_f32(uint8_t nibble);
 int orc_mx8_exponent(float amax);            /* ceil(log2(amax/448)) clamped, 0 for amax 0 */
 long long orc_sf_tiled_offset(long long r, int kb, int kg4);
+/* tile-major GEMM operands (128 x 128-element tiles, tile (r/128, k/128) at
+ * index (r/128)*(K/128) + k/128, row-major inside): byte of E4M3 element (r, k),
+ * byte of packed E2M1 element (r, k) */
+long long orc_op8_offset(long long r, int k, int K);
+long long orc_op4_offset(long long r, int k, int K);
 
 /* router top-k: source/k3_moe_route.cu:117-221, 372-385; source/k3_prefill_glue.cu:504-557 */
 void orc_topk(const float* S, int lds, const float* bias, uint16_t rs_bits, int T, int E, int K, int32_t* idx,

@@ -80,6 +80,14 @@ long long orc_sf_tiled_offset(long long r, int kb, int kg4) {
   return ((r / 128) * kg4 + kb / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + kb % 4;
 }
 
+long long orc_op8_offset(long long r, int k, int K) {
+  return ((r / 128) * (K / 128) + k / 128) * 16384 + (r % 128) * 128 + k % 128;
+}
+
+long long orc_op4_offset(long long r, int k, int K) {
+  return ((r / 128) * (K / 128) + k / 128) * 8192 + (r % 128) * 64 + (k % 128) / 2;
+}
+
 static uint32_t ord_f32(float f) {
   uint32_t b;
   memcpy(&b, &f, 4);
@@ -211,7 +219,7 @@ void orc_quant_permute(const uint16_t* x, int ldx, int R, int cols, int K, const
     for (int kb = 0; kb < kbn; ++kb) {
       const uint8_t s = quant_group(x + (size_t)r * ldx + kb * 32, qg);
       for (int d = 0; d < nd; ++d) {
-        memcpy(q_perm + (size_t)dst[d] * cols + kb * 32, qg, 32);
+        memcpy(q_perm + orc_op8_offset(dst[d], kb * 32, cols), qg, 32);
         sf_perm[orc_sf_tiled_offset(dst[d], kb, kg4)] = s;
       }
     }
@@ -250,7 +258,7 @@ void orc_quant_mxfp4(const float* w, long long rows, int K, uint8_t* packed, uin
         if (X < -127) X = -127;
         if (X > 127) X = 127;
       }
-      uint8_t* out = packed + r * (K / 2) + kb * 16;
+      uint8_t* out = packed + orc_op4_offset(r, kb * 32, K);
       for (int j = 0; j < 16; ++j) {
         const uint8_t lo = e2m1_round(ldexpf(v[2 * j], -X));
         const uint8_t hi = e2m1_round(ldexpf(v[2 * j + 1], -X));

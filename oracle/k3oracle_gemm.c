@@ -16,11 +16,11 @@ static float ue8m0(uint8_t s) { return s == 255 ? NAN : ldexpf(1.0f, (int)s - 12
 /* weight row r (flattened over experts) of K elements -> f32 */
 static void dequant_w_row(const uint8_t* w, const uint8_t* w_sf, long long r, int K, float* out) {
   const int kg4 = (K / 32 + 3) / 4;
-  const uint8_t* row = w + r * (K / 2);
   for (int kb = 0; kb < K / 32; ++kb) {
     const float s = ue8m0(w_sf[orc_sf_tiled_offset(r, kb, kg4)]);
+    const uint8_t* grp = w + orc_op4_offset(r, kb * 32, K);
     for (int j = 0; j < 16; ++j) {
-      const uint8_t b = row[kb * 16 + j];
+      const uint8_t b = grp[j];
       out[kb * 32 + 2 * j] = orc_e2m1_to_f32(b & 15) * s;
       out[kb * 32 + 2 * j + 1] = orc_e2m1_to_f32(b >> 4) * s;
     }
@@ -32,7 +32,8 @@ static void dequant_a_row(const uint8_t* q, const uint8_t* sf, long long p, int 
   const int kg4 = (K / 32 + 3) / 4;
   for (int kb = 0; kb < K / 32; ++kb) {
     const float s = ue8m0(sf[orc_sf_tiled_offset(p, kb, kg4)]);
-    for (int j = 0; j < 32; ++j) out[kb * 32 + j] = orc_e4m3_to_f32(q[p * K + kb * 32 + j]) * s;
+    const uint8_t* grp = q + orc_op8_offset(p, kb * 32, K);
+    for (int j = 0; j < 32; ++j) out[kb * 32 + j] = orc_e4m3_to_f32(grp[j]) * s;
   }
 }
 
@@ -84,8 +85,8 @@ void orc_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, c
         }
         const int ex = orc_mx8_exponent(amax);
         const float s = ldexpf(1.0f, -ex);
-        for (int i = 0; i < 32; ++i)
-          fc1_q[(size_t)(row0 + j) * I + kb * 32 + i] = orc_f32_to_e4m3_sat(h[(size_t)j * I + kb * 32 + i] * s);
+        uint8_t* grp = fc1_q + orc_op8_offset(row0 + j, kb * 32, I);
+        for (int i = 0; i < 32; ++i) grp[i] = orc_f32_to_e4m3_sat(h[(size_t)j * I + kb * 32 + i] * s);
         fc1_sf[orc_sf_tiled_offset(row0 + j, kb, kg4_out)] = (uint8_t)(ex + 127);
       }
     free(act);

@@ -167,15 +167,24 @@ def e4m3_to_f32(q: np.ndarray) -> np.ndarray:
     return E4M3_TABLE[q]
 
 
+def t128_rows(buf: np.ndarray, rows, K: int) -> np.ndarray:
+    """Rows of a tile-major E4M3 operand (128 x 128 tiles, see k3oracle.h) as row-major [len(rows), K]."""
+    flat = np.ascontiguousarray(buf).reshape(-1)
+    r = np.asarray(rows, np.int64)[:, None]
+    k = np.arange(K, dtype=np.int64)[None, :]
+    off = ((r // 128) * (K // 128) + k // 128) * 16384 + (r % 128) * 128 + k % 128
+    return flat[off]
+
+
 def dequant_rows(q: np.ndarray, sf_tiled: np.ndarray, rows: np.ndarray) -> np.ndarray:
-    """MXFP8 rows (tiled scales) -> f32 [len(rows), cols]."""
+    """MXFP8 rows of a tile-major operand (tiled scales) -> f32 [len(rows), cols]."""
     cols = q.shape[1]
     kbn, kg4 = cols // 32, -(-cols // 128)
     r = rows.astype(np.int64)[:, None]
     kb = np.arange(kbn, dtype=np.int64)[None, :]
     off = ((r // 128) * kg4 + kb // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + kb % 4
     s = np.ldexp(np.float32(1.0), sf_tiled[off].astype(np.int32) - 127).astype(np.float32)
-    v = e4m3_to_f32(q[rows]).reshape(len(rows), kbn, 32)
+    v = e4m3_to_f32(t128_rows(q, rows, cols)).reshape(len(rows), kbn, 32)
     return (v * s[:, :, None]).reshape(len(rows), cols)
 
 
