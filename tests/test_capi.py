@@ -1,0 +1,62 @@
+"""CPU tests of the C ABI boundary (no GPU work is launched): the library
+loads, exports every entry point include/k3moe.h declares, and rejects bad
+arguments before touching the device."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "k3moe.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import __graft_entry__
+
+    __graft_entry__.build()
+    import k3moe
+
+    return k3moe.lib()
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(k3moe_\w+)\s*\(", src)))
+
+
+def test_header_declares_entries():
+    names = declared()
+    assert "k3moe_layer_forward" in names and "k3moe_fc1" in names and len(names) >= 15
+
+
+def test_library_exports_every_declared_symbol(lib):
+    import k3moe
+
+    nm = subprocess.run(["nm", "-D", "--defined-only", k3moe.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (k3moe_\w+)", nm))
+    missing = [n for n in declared() if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    # every declared entry is also bound (with its signature) by the Python mirror
+    assert sorted(k3moe.SIGNATURES) == declared()
+
+
+def test_pure_host_entries(lib):
+    assert lib.k3moe_abi_version() == 1
+    assert lib.k3moe_max_ctas(8192, 8, 896, 1, 128) == 897 + (8192 * 9 + 127) // 128
+    ws = lib.k3moe_layer_workspace_size(8192, 7168, 2048, 896, 8, 1)
+    assert ws > 3 * 10 ** 9
+    off = (ctypes.c_size_t * 14)()
+    assert lib.k3moe_layer_workspace_offsets(8192, 7168, 2048, 896, 8, 1, ctypes.cast(off, ctypes.c_void_p)) == 0
+    assert list(off) == sorted(off) and off[-1] < ws
+
+
+def test_bad_arguments_rejected_without_device_work(lib):
+    # K not a power of two / too many experts / bad widths: rejected before any launch
+    assert lib.k3moe_route_topk(None, 896, None, None, 8, 896, 3, None, None, None) == -1
+    assert lib.k3moe_route_topk(None, 2048, None, None, 8, 2048, 8, None, None, None) == -1
+    assert lib.k3moe_quant_mxfp8(None, 100, 4, 100, None, None, 0, None) == -1
+    assert lib.k3moe_layer_forward(None, None, 0, None) == -1
