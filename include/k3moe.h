@@ -49,7 +49,8 @@ enum {
   K3MOE_EDRIVER = -3,    /* the CUDA driver entry for tensor maps is unavailable */
   K3MOE_ETMAP = -4,      /* a tensor map could not be encoded (alignment / size) */
   K3MOE_ELAUNCH = -5,    /* a kernel launch failed (cudaGetLastError) */
-  K3MOE_EDEVICE = -6     /* k3moe_read_error: the device reported a failure */
+  K3MOE_EDEVICE = -6,    /* k3moe_read_error: the device reported a failure */
+  K3MOE_ELIMIT = -7      /* a size beyond the fixed scratch of k3moe_route_tables_noalloc */
 };
 
 /* Version of this ABI. */
@@ -84,6 +85,22 @@ int k3moe_route_tables(const int32_t* idx, int R, int K, int first, int E, int s
 
 /* Capacity bounds of the tables: CTAs <= E + shared + ceil((R*K + shared*R) / tile). */
 int k3moe_max_ctas(int R, int K, int E, int shared, int tile);
+
+/* k3moe_route_tables for callers that cannot allocate device memory (a host
+ * runtime that owns all device buffers and binds a fixed list to each call, or
+ * a latency-critical loop that cannot afford cudaMalloc's possible device-wide
+ * synchronisation): the same tables, with the scratch taken from an array
+ * compiled into the library instead of a caller buffer; nothing is allocated.
+ * Limits: R <= K3MOE_NOALLOC_MAX_ROWS and E + shared <= K3MOE_NOALLOC_MAX_EXPERTS,
+ * else K3MOE_ELIMIT.  The array (513 KB) is one per device and shared by every
+ * call: calls that overlap on the GPU race on it.  The first call on a device
+ * looks the array up (make it before any stream capture).
+ * No counterpart in the reference: it has no allocation-free variant. */
+#define K3MOE_NOALLOC_MAX_ROWS 16384
+#define K3MOE_NOALLOC_MAX_EXPERTS 1025
+int k3moe_route_tables_noalloc(const int32_t* idx, int R, int K, int first, int E, int shared, int tile,
+                               int32_t* counts, int32_t* cta_batch, int32_t* cta_limit, int32_t* meta,
+                               int32_t* route_map, int32_t* exp2perm, k3moe_stream_t stream);
 
 /* ---------------------------------------------------------------- MXFP8 quantisation
  * Per 32 elements along a row: e = ceil(log2(amax/448)) (0 when amax is 0),

@@ -378,3 +378,5 @@ int k3moe_read_error(uint32_t* err, uint32_t* out2, int clear, k3moe_stream_t st
 }
 
 }  // extern "C"
+
+#include "noalloc.cu"

@@ -25,6 +25,7 @@ _ERRORS = {
     -4: "tensor map could not be encoded (alignment / size)",
     -5: "kernel launch failed",
     -6: "device reported an error",
+    -7: "size beyond the fixed scratch of the allocation-free entry",
 }
 
 # (name, restype, argtypes) of every exported entry point; tests check the
@@ -49,6 +50,7 @@ SIGNATURES = {
     "k3moe_layer_workspace_offsets": (_I, [_I, _I, _I, _I, _I, _I, _P]),
     "k3moe_read_error": (_I, [_P, _P, _I, _P]),
     "k3moe_set_trace": (_I, [_P]),
+    "k3moe_route_tables_noalloc": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",
@@ -150,6 +152,32 @@ def route_tables(idx: torch.Tensor, E: int, first: int = 0, shared: int = 0, til
     _check(L.k3moe_route_tables(_p(idx), R, K, first, E, shared, tile, _p(scratch), _p(t.counts), _p(t.cta_batch),
                                 _p(t.cta_limit), _p(t.meta), _p(t.route_map), _p(t.exp2perm), _stream(stream)),
            "route_tables")
+    return t
+
+
+NOALLOC_MAX_ROWS, NOALLOC_MAX_EXPERTS = 16384, 1025  # include/k3moe.h
+
+
+def route_tables_noalloc(idx: torch.Tensor, E: int, first: int = 0, shared: int = 0, tile: int = 128,
+                         stream=None, out: Tables | None = None) -> Tables:
+    """route_tables() through k3moe_route_tables_noalloc: the library allocates nothing (its scratch is a fixed
+    array in the library; see include/k3moe.h).  `out` may hold preallocated output tables."""
+    R, K = idx.shape
+    L = lib()
+    max_ctas = L.k3moe_max_ctas(R, K, E, shared, tile)
+    cap = max_ctas * tile
+    dev = idx.device
+    t = out or Tables(
+        counts=torch.empty(E + shared, dtype=torch.int32, device=dev),
+        cta_batch=torch.empty(max_ctas, dtype=torch.int32, device=dev),
+        cta_limit=torch.empty(max_ctas, dtype=torch.int32, device=dev),
+        meta=torch.zeros(4, dtype=torch.int32, device=dev),
+        route_map=torch.empty(cap, dtype=torch.int32, device=dev),
+        exp2perm=torch.empty((R, K), dtype=torch.int32, device=dev),
+        max_ctas=max_ctas, cap_rows=cap)
+    _check(L.k3moe_route_tables_noalloc(_p(idx), R, K, first, E, shared, tile, _p(t.counts), _p(t.cta_batch),
+                                        _p(t.cta_limit), _p(t.meta), _p(t.route_map), _p(t.exp2perm),
+                                        _stream(stream)), "route_tables_noalloc")
     return t
 
 
