@@ -13,9 +13,10 @@ dataset).  The router logits S = x.W_router are computed once before timing
 
 `value` is device-resident throughput (tokens/s over all ranks); `e2e` is the
 same layer through the public API with x and S copied from pinned host memory
-and the output copied back inside every timed step.  With N > 1 every rank
-runs its own 8192-row chunk through all 896 experts (the experts replicated
-per GPU, no data-path collective; weak scaling).  `--impl reference` times the
+and the output copied back inside every timed step.  With N > 1 the layer is
+expert parallel (config 4's layout): every rank owns an 8192-row chunk and
+896/N experts (+ the shared expert), tokens travel to their experts' ranks and
+back by NCCL all-to-all (timed separately), weak scaling.  `--impl reference` times the
 CPU restatement of the same path (oracle/, the reference's algorithm) on a
 bounded sample on the host cores.
 """
@@ -221,6 +222,113 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ the GPU arm, N > 1: expert parallel
+def run_ep(args, world, rank, dev):
+    """Config 4's layout at N GPUs: every rank owns an 8192-row chunk (16 packed sequences) and E/N experts
+    (+ the shared expert); dispatch and combine are NCCL all-to-all; weak scaling (N x 8192 rows a step)."""
+    import torch
+    import torch.distributed as dist
+
+    import k3moe
+    import k3moe_ep
+
+    E, T = args.experts, args.tokens
+    El = E // world
+    e0 = rank * El
+    # this rank's weights only: its routed experts then the shared expert (the same synthetic stream as N = 1)
+    w = {}
+    for name, rows_per, K_, seed in (("w13", 2 * I, H, W_SEED13), ("w2", H, I, W_SEED2)):
+        packed = torch.empty(((El + SHARED) * rows_per, K_ // 2), dtype=torch.uint8, device=dev)
+        sf = torch.zeros((El + SHARED) * rows_per // 128 * (K_ // 128) * 512, dtype=torch.uint8, device=dev)
+        per_sf = rows_per // 128 * (K_ // 128) * 512
+        k3moe.synth_mxfp4(seed, El * rows_per, K_, WSD, row0=e0 * rows_per, packed=packed[:El * rows_per],
+                          sf=sf[:El * per_sf])
+        k3moe.synth_mxfp4(seed, rows_per, K_, WSD, row0=E * rows_per, packed=packed[El * rows_per:],
+                          sf=sf[El * per_sf:])
+        w[name], w[name + "_sf"] = packed, sf
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn((T, H), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    g.manual_seed(7)
+    wr = torch.randn((H, E), generator=g, device=dev, dtype=torch.float32) / H ** 0.5
+    S = (x.float() @ wr).contiguous()
+    bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
+    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
+    del wr
+    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev)
+    for _ in range(args.warmup):
+        layer.forward(S, x)
+    torch.cuda.synchronize()
+    names = ("dispatch", "fc1", "combine")
+    evs = [{n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
+           for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clk:
+        start.record()
+        for s in range(args.steps):
+            layer.forward(S, x, evs[s])
+        stop.record()
+        torch.cuda.synchronize()
+    dist.barrier()
+    ms = start.elapsed_time(stop) / args.steps
+    part = {n: float(np.mean([e[n][0].elapsed_time(e[n][1]) for e in evs])) for n in names}
+    t = torch.tensor([ms, part["dispatch"], part["combine"], part["fc1"]], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, disp_ms, comb_ms, fc1_ms = [float(v) for v in t.tolist()]
+    # e2e: x and S from pinned host memory in, the output back, every step
+    x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
+    out_h = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xd, Sd = torch.empty_like(x), torch.empty_like(S)
+    dist.barrier()
+    e0v, e1v = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = args.e2e_steps or args.steps
+    e0v.record()
+    for _ in range(n_e2e):
+        xd.copy_(x_h, non_blocking=True)
+        Sd.copy_(S_h, non_blocking=True)
+        out = layer.forward(Sd, xd)
+        out_h.copy_(out, non_blocking=True)
+    e1v.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0v.elapsed_time(e1v) / n_e2e], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    tb = layer.last["tables"]
+    counts = tb.counts.cpu().numpy()
+    routed_rows, touched = int(counts.sum()), int((counts > 0).sum())
+    fc1_bytes = touched * (2 * I * H // 2 + 2 * I * H // 32) + routed_rows * (H + H // 32 + I + I // 32)
+    hbm_peak, peak_kind = peaks()
+    if rank == 0:
+        flops = layer_flops(T) * world
+        achieved = fc1_bytes / (fc1_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"K3-shape prefill MoE layer, expert parallel over {world} GPUs (config 4 layout)",
+                       "T_per_gpu": T, "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I,
+                       "rs": RS, "global_batch": T * world, "seq_len": T, "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2: each GPU streams its experts' weights every step"},
+            "tflops": flops / (ms / 1e3) / 1e12,
+            "a2a_ms": {"dispatch": disp_ms, "combine": comb_ms},
+            "roofline": {"kernel": "FC1 grouped GEMM (grouped_gemm_kernel<0>), rank 0", "bound": "hbm",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes, "traffic": None},
+            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4) * world,
+                    "d2h_bytes_per_step": int(x.numel() * 2) * world},
+            "gpu_launches": 14 * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ the GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -251,6 +359,7 @@ def main():
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        return run_ep(args, world, rank, dev)
     E = args.experts  # noqa: N806  (the routed experts of this run; smaller only for profiling captures)
     T = args.tokens
     k3moe.lib()
@@ -299,6 +408,24 @@ def main():
     torch.cuda.synchronize()
     layer.check_device_error(T)
     ms = start.elapsed_time(stop) / args.steps
+    # GEMM role counters over 2 extra (untimed) steps: where each role of FC1 / FC2 spends its cycles
+    trace = torch.zeros(32, dtype=torch.int64, device=dev)
+    k3moe.set_trace(trace)
+    for _ in range(2):
+        layer.forward(S, x, out)
+    torch.cuda.synchronize()
+    k3moe.set_trace(None)
+    tr = trace.cpu().tolist()
+    gemm_trace = {}
+    for mode, name in ((0, "fc1"), (1, "fc2")):
+        c = dict(zip(k3moe.TRACE_FIELDS, tr[16 * mode:16 * mode + 8]))
+        gemm_trace[name] = {
+            "mma_busy": round(1 - (c["mma_wait_loaded"] + c["mma_wait_drained"]) / max(c["mma"], 1), 3),
+            "mma_wait_loaded": round(c["mma_wait_loaded"] / max(c["mma"], 1), 3),
+            "mma_wait_drained": round(c["mma_wait_drained"] / max(c["mma"], 1), 3),
+            "producer_wait_stage": round(c["producer_wait_stage"] / max(c["producer"], 1), 3),
+            "epilogue_busy": round(1 - c["epilogue_wait_acc"] / max(c["epilogue"], 1), 3),
+        }
     stage_ms = np.array([[ev[s][i].elapsed_time(ev[s][i + 1]) for i in range(6)] for s in range(args.steps)]).mean(0)
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -319,12 +446,14 @@ def main():
     fc1_ms = float(stage_ms[3])
     hbm_peak, peak_kind = peaks()
     achieved = fc1_bytes / (fc1_ms / 1e3) / 1e9
+    # DRAM bytes (read + write) of one FC1 launch of this workload, from the ncu capture summarised in
+    # profiles/grouped_gemm_fc1_config1_traffic.md (line "bytes_per_launch: N")
     traffic = None
-    tf = os.path.join(ROOT, "profiles", "fc1_traffic.json")
-    if os.path.exists(tf):
-        with open(tf) as f:
-            tr = json.load(f)
-        traffic = tr.get("bytes_per_launch")
+    tf = os.path.join(ROOT, "profiles", "grouped_gemm_fc1_config1_traffic.md")
+    if os.path.exists(tf) and T == T_DEF and E == 896:
+        for ln in open(tf):
+            if ln.startswith("bytes_per_launch:"):
+                traffic = int(ln.split(":")[1].strip())
 
     # ---------------- end to end through the public API: host x/S in, host out back
     e2e_steps = args.e2e_steps or args.steps
@@ -415,6 +544,7 @@ def main():
                     "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
                     "d2h_bytes_per_step": int(out.numel() * 2)},
             "gpu_launches": 8 * args.steps,
+            "gemm_trace": gemm_trace,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }

@@ -73,7 +73,10 @@ int k3moe_route_topk(const float* S, int lds, const float* bias, const void* rs_
  * row of the shared expert (or -1), route_map[perm] = row (padding rows 0),
  * exp2perm[r*K + k] = perm or -1 (foreign expert).  With shared = 1 a further
  * local expert E takes every row.  Within an expert the rows are in row
- * order, so the tables are the same bytes on every run.
+ * order, so the tables are the same bytes on every run.  The K ids of one row
+ * must be distinct (as top-k ids are); to rank repeated ids (e.g. destination
+ * ranks), pass them one a row (K = 1).  tile = 1 plans positions only (no CTA
+ * tables are written).
  * scratch: k3moe_route_scratch_bytes(R, E, shared) bytes.  E + shared <= 2048.
  * Replaces: kern_k3_moe_route_count / _tables / _scatter
  *   (source/k3_moe_prefill.cu:97-204), phase 2 of kern_k3g_moe_route
@@ -134,6 +137,34 @@ int k3moe_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, 
 int k3moe_fc2(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
               const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, void* fc2_bf16, int H, int I,
               int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream);
+
+/* FC2 storing permuted row r at row out_rows[r] of fc2_bf16 (the expert-parallel
+ * layer passes route_map, so rows come out in the order they were received). */
+int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+                      const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const int32_t* out_rows,
+                      void* fc2_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
+                      k3moe_stream_t stream);
+
+/* ---------------------------------------------------------------- expert parallelism
+ * Tokens are owned by their rank; experts are split in contiguous blocks of
+ * E_local.  A routed pick travels as one packed row (dispatch wire format) of
+ * k3moe_ep_row_stride(H) bytes: E4M3 [H] | UE8M0 [H/32] | int32 local expert id.
+ * No counterpart in the reference for the MoE (its decode EP replicates the
+ * batch and all-reduces: roofline/decode.md:164-166; k3_ar_fused.cu:916). */
+int k3moe_ep_row_stride(int H);
+/* Quantise row t of x once and write it to send slots send_pos[t*K + k] (>= 0)
+ * with id idx % E_local; with send_pos null, to slot t with id fixed_eid. */
+int k3moe_ep_pack(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* idx, const int32_t* send_pos,
+                  int E_local, int fixed_eid, uint8_t* dst, int stride, k3moe_stream_t stream);
+/* ids[i] = the local expert id of packed row i. */
+int k3moe_ep_ids(const uint8_t* rows, int stride, int R, int H, int32_t* ids, k3moe_stream_t stream);
+/* Packed row i -> permuted row perm[i] (>= 0) of the GEMM operand (tile-major q, tiled scales). */
+int k3moe_ep_unpack(const uint8_t* rows, int stride, int R, int H, const int32_t* perm, uint8_t* q_perm,
+                    uint8_t* sf_perm, k3moe_stream_t stream);
+/* out[t] = bf16( sum_k fma(wts[t,k], back[pos[t,k]], acc) (pos >= 0, k in order) + shared[t] ):
+ * the combine over rows returned by the combine all-to-all (shared_bf16 may be null). */
+int k3moe_combine_ep(const void* back_bf16, const int32_t* pos, const float* wts, const void* shared_bf16,
+                     int ld_shared, void* out_bf16, int ldo, int T, int K, int cols, k3moe_stream_t stream);
 
 /* ---------------------------------------------------------------- combine
  * out[t] = bf16( sum over k = 0..K-1 with exp2perm >= 0 of fma(wts, fc2[p], acc)

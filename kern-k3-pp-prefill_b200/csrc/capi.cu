@@ -9,6 +9,7 @@
 #include "../../include/k3moe.h"
 #include "gemm.cu"
 #include "route.cu"
+#include "ep.cu"
 
 using namespace k3;
 
@@ -98,7 +99,7 @@ void launch_topk(const float* S, int lds, const float* bias, const bf16* rs, int
 int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* act, const uint8_t* act_sf,
                 const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* out_q,
                 uint8_t* out_sf, void* out_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas,
-                uint32_t* err, cudaStream_t stream) {
+                uint32_t* err, cudaStream_t stream, const int32_t* out_rows = nullptr) {
   if (H <= 0 || I <= 0 || H % 256 || I % 256 || n_experts <= 0 || cap_rows <= 0 || cap_rows % 128 || max_ctas <= 0 ||
       (long long)max_ctas * 128 > cap_rows)
     return K3MOE_EINVAL;
@@ -118,6 +119,7 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   p.out_q = out_q;
   p.out_sf = out_sf;
   p.out_bf16 = reinterpret_cast<bf16*>(out_bf16);
+  p.out_rows = out_rows;
   p.err = err;
   p.K = K;
   p.rows_per_expert = rows_per_expert;
@@ -219,7 +221,7 @@ int k3moe_route_tables(const int32_t* idx, int R, int K, int first, int E, int s
                        int32_t* counts, int32_t* cta_batch, int32_t* cta_limit, int32_t* meta, int32_t* route_map,
                        int32_t* exp2perm, k3moe_stream_t stream) {
   shared = shared ? 1 : 0;
-  if (R < 1 || K < 1 || K > 16 || E < 1 || E + shared > 2048 || tile < 8 || tile > 1024) return K3MOE_EINVAL;
+  if (R < 1 || K < 1 || K > 16 || E < 1 || E + shared > 2048 || tile < 1 || tile > 1024) return K3MOE_EINVAL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int nb = (int)cdiv(R, TB), EL = E + shared;
   int* blockcount = reinterpret_cast<int*>(scratch);
@@ -361,6 +363,57 @@ int k3moe_layer_forward_events(const k3moe_layer_args* a, void* workspace, size_
 
 int k3moe_layer_forward(const k3moe_layer_args* a, void* workspace, size_t ws_bytes, k3moe_stream_t stream) {
   return k3moe_layer_forward_events(a, workspace, ws_bytes, stream, nullptr, 0);
+}
+
+int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+                      const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const int32_t* out_rows,
+                      void* out_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
+                      k3moe_stream_t stream) {
+  if (!out_rows) return K3MOE_EINVAL;
+  return gemm_launch(MODE_FC2, w2, w2_sf, fc1_q, fc1_sf, cta_batch, cta_limit, meta, nullptr, nullptr, out_bf16, H, I,
+                     n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream), out_rows);
+}
+
+int k3moe_ep_row_stride(int H) { return H > 0 && H % 256 == 0 ? (H + H / 32 + 4 + 15) / 16 * 16 : 0; }
+
+int k3moe_ep_pack(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* idx, const int32_t* send_pos,
+                  int E_local, int fixed_eid, uint8_t* dst, int stride, k3moe_stream_t stream) {
+  if (T < 0 || H <= 0 || H % 256 || ldx < H || ldx % 8 || stride < k3moe_ep_row_stride(H) || stride % 16 ||
+      (send_pos && (K < 1 || K > 16 || !idx || E_local < 1)))
+    return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  const int grid = (int)std::min<long long>(cdiv(T, 8), (long long)num_sms(current_device()) * 8);
+  ep_pack_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, idx, send_pos, E_local, fixed_eid, dst, stride);
+  return launch_status();
+}
+
+int k3moe_ep_ids(const uint8_t* rows, int stride, int R, int H, int32_t* ids, k3moe_stream_t stream) {
+  if (R < 0 || H <= 0 || stride < k3moe_ep_row_stride(H)) return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  ep_ids_kernel<<<(unsigned)cdiv(R, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(rows, stride, R, H, ids);
+  return launch_status();
+}
+
+int k3moe_ep_unpack(const uint8_t* rows, int stride, int R, int H, const int32_t* perm, uint8_t* q_perm,
+                    uint8_t* sf_perm, k3moe_stream_t stream) {
+  if (R < 0 || H <= 0 || H % 256 || stride < k3moe_ep_row_stride(H) || stride % 16) return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  const int grid = (int)std::min<long long>(cdiv(R, 8), (long long)num_sms(current_device()) * 8);
+  ep_unpack_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(rows, stride, R, H, perm, q_perm, sf_perm);
+  return launch_status();
+}
+
+int k3moe_combine_ep(const void* back_bf16, const int32_t* pos, const float* wts, const void* shared_bf16,
+                     int ld_shared, void* out_bf16, int ldo, int T, int K, int cols, k3moe_stream_t stream) {
+  if (T < 0 || K < 1 || K > 16 || cols <= 0 || cols % 8 || ldo < cols || ldo % 8 ||
+      (shared_bf16 && (ld_shared < cols || ld_shared % 8)))
+    return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  combine_ep_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(back_bf16), pos, wts, reinterpret_cast<const bf16*>(shared_bf16), ld_shared,
+      reinterpret_cast<bf16*>(out_bf16), ldo, T, K, cols);
+  return launch_status();
 }
 
 int k3moe_set_trace(uint64_t* counters) {

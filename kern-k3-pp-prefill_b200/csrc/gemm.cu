@@ -68,6 +68,7 @@ struct GemmParams {
   uint8_t* out_q;           // FC1: [cap_rows, out_cols] E4M3, tile-major
   uint8_t* out_sf;          // FC1: tiled scales over permuted rows
   bf16* out_bf16;           // FC2: [cap_rows, out_cols] row-major
+  const int* out_rows;      // FC2: permuted row r is stored at row out_rows[r] (null: at r)
   u32* err;
   int K;                    // reduction length (elements), multiple of 128
   int rows_per_expert;      // weight rows an expert: FC1 2I, FC2 H
@@ -353,7 +354,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           const int kb = (w.fb * 128 + 64 * half) / 32;
           *reinterpret_cast<unsigned short*>(p.out_sf + sf_tiled_offset(r, kb, kg4)) = (unsigned short)sfw;
         } else {
-          bf16* dst = p.out_bf16 + r * p.out_cols + w.fb * BN + 128 * half;
+          const long long ro = p.out_rows ? (long long)p.out_rows[r] : r;
+          bf16* dst = p.out_bf16 + ro * p.out_cols + w.fb * BN + 128 * half;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
 #pragma unroll

@@ -169,7 +169,8 @@ __global__ void __launch_bounds__(1024) route_tables_kernel(const int* __restric
   }
   for (int e = t; e < EL; e += blockDim.x) {
     const int o = s_off[e], n = s_off[e + 1] - o, cnt = s_cnt[e];
-    for (int c = 0; c < n; ++c) {
+    // tile 1 plans positions only (the all-to-all send order): no CTA tables
+    for (int c = 0; c < n && tile > 1; ++c) {
       cta_batch[o + c] = e;
       cta_limit[o + c] = min((o + c + 1) * tile, o * tile + cnt);
     }

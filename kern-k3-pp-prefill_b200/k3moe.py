@@ -51,6 +51,12 @@ SIGNATURES = {
     "k3moe_read_error": (_I, [_P, _P, _I, _P]),
     "k3moe_set_trace": (_I, [_P]),
     "k3moe_route_tables_noalloc": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "k3moe_fc2_to_rows": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "k3moe_ep_row_stride": (_I, [_I]),
+    "k3moe_ep_pack": (_I, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
+    "k3moe_ep_ids": (_I, [_P, _I, _I, _I, _P, _P]),
+    "k3moe_ep_unpack": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
+    "k3moe_combine_ep": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",

@@ -1,0 +1,184 @@
+"""Expert-parallel routed-MoE layer: one process a GPU, experts split in
+contiguous blocks, tokens owned by their rank, dispatch and combine as NCCL
+all-to-all (torch.distributed for the plumbing; the only collective of the path).
+
+Per rank (world W, E_local = E / W experts, T local tokens):
+
+1. router top-k on the local tokens (global expert ids);
+2. a send plan: each pick's destination rank = id // E_local; the routing-table
+   builder with tile 1, run over the expanded (token, k) picks, gives every pick
+   a send slot, grouped by destination and in (token, k) order within one
+   (deterministic), and the per-destination counts;
+3. pack: each token quantised to MXFP8 once and written to its slots as packed
+   rows (E4M3 | UE8M0 | local expert id);
+4. counts all-to-all (the one host synchronisation), then the dispatch
+   all-to-all of packed rows; the local tokens are appended for the shared
+   expert, which every rank holds (local expert E_local);
+5. routing tables over the received rows (K = 1), unpack into the GEMM operand,
+   FC1, FC2 with rows stored back in the order they were received;
+6. the combine all-to-all sends each result row back to its owner, which sums
+   its K rows in k order with f32 FMAs plus the shared row: the single-GPU
+   combine's arithmetic, so the layer's output is bit-identical to one GPU
+   holding every expert.
+
+The reference has no MoE all-to-all (its decode EP replicates the batch and
+all-reduces, roofline/decode.md:164-166); this is the token-sharded layout of
+the benchmark configurations.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+import k3moe
+
+
+class GpuOps:
+    """The path's steps on the GPU (libk3moe.so through the C ABI)."""
+
+    def __init__(self, device):
+        self.device = device
+        self.err = torch.zeros(4, dtype=torch.int32, device=device)
+
+    def topk(self, S, bias, rs, K):
+        return k3moe.route_topk(S, bias, rs, K)
+
+    def tables(self, ids, E, tile):
+        return k3moe.route_tables(ids, E, 0, 0, tile)
+
+    def stride(self, H):
+        return k3moe.lib().k3moe_ep_row_stride(H)
+
+    def pack(self, x, idx, send_pos, E_local, n_slots):
+        H = x.shape[1]
+        st = self.stride(H)
+        buf = torch.empty((n_slots, st), dtype=torch.uint8, device=x.device)
+        k3moe._check(k3moe.lib().k3moe_ep_pack(x.data_ptr(), x.stride(0), x.shape[0], H, idx.shape[1], idx.data_ptr(),
+                                               send_pos.data_ptr(), E_local, 0, buf.data_ptr(), st,
+                                               k3moe._stream()), "ep_pack")
+        return buf
+
+    def pack_rows(self, x, eid, dst):
+        H = x.shape[1]
+        k3moe._check(k3moe.lib().k3moe_ep_pack(x.data_ptr(), x.stride(0), x.shape[0], H, 1, None, None, 1, eid,
+                                               dst.data_ptr(), dst.shape[1], k3moe._stream()), "ep_pack_rows")
+
+    def ids(self, rows, R, H):
+        ids = torch.empty((R, 1), dtype=torch.int32, device=rows.device)
+        k3moe._check(k3moe.lib().k3moe_ep_ids(rows.data_ptr(), rows.shape[1], R, H, ids.data_ptr(),
+                                              k3moe._stream()), "ep_ids")
+        return ids
+
+    def unpack(self, rows, R, H, tb):
+        qp = torch.empty((tb.cap_rows, H), dtype=torch.uint8, device=rows.device)
+        sfp = torch.zeros(tb.cap_rows * H // 32, dtype=torch.uint8, device=rows.device)
+        k3moe._check(k3moe.lib().k3moe_ep_unpack(rows.data_ptr(), rows.shape[1], R, H, tb.exp2perm.data_ptr(),
+                                                 qp.data_ptr(), sfp.data_ptr(), k3moe._stream()), "ep_unpack")
+        return qp, sfp
+
+    def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None):
+        if events:
+            events["fc1"][0].record()
+        f1q, f1sf = k3moe.fc1(w["w13"], w["w13_sf"], qp, sfp, tb, H, I, n_experts, self.err)
+        if events:
+            events["fc1"][1].record()
+        y = torch.empty((n_rows, H), dtype=torch.bfloat16, device=qp.device)
+        k3moe._check(k3moe.lib().k3moe_fc2_to_rows(
+            w["w2"].data_ptr(), w["w2_sf"].data_ptr(), f1q.data_ptr(), f1sf.data_ptr(), tb.cta_batch.data_ptr(),
+            tb.cta_limit.data_ptr(), tb.meta.data_ptr(), tb.route_map.data_ptr(), y.data_ptr(), H, I, n_experts,
+            tb.cap_rows, tb.max_ctas, self.err.data_ptr(), k3moe._stream()), "fc2_to_rows")
+        return y
+
+    def combine(self, back, send_pos, wts, shared_rows, T, K, H):
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=back.device)
+        sp = shared_rows.data_ptr() if shared_rows is not None else None
+        ld = shared_rows.stride(0) if shared_rows is not None else 0
+        k3moe._check(k3moe.lib().k3moe_combine_ep(back.data_ptr(), send_pos.data_ptr(), wts.data_ptr(), sp, ld,
+                                                  out.data_ptr(), H, T, K, H, k3moe._stream()), "combine_ep")
+        return out
+
+
+class EPMoELayer:
+    """One rank's part of an expert-parallel MoE layer.
+
+    w: this rank's weights {w13, w13_sf, w2, w2_sf} holding its E_local routed experts (global ids
+    [rank*E_local, (rank+1)*E_local)) and, with `shared`, the shared expert as local expert E_local.
+    """
+
+    def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if E % self.world:
+            raise ValueError(f"{E} experts do not split over {self.world} ranks")
+        self.H, self.I, self.E, self.K, self.shared = H, I, E, K, int(shared)
+        self.E_local = E // self.world
+        self.w, self.bias, self.rs = w, bias, rs
+        self.ops = ops or GpuOps(device)
+        self.timing = None  # (dispatch_ms, combine_ms) of the last forward when events are given
+
+    def _a2a(self, out, inp, out_rows, in_rows):
+        """All-to-all of whole rows as bytes (every backend moves uint8); splits in rows."""
+        ob = out.reshape(-1).view(torch.uint8)
+        ib = inp.reshape(-1).view(torch.uint8)
+        row_bytes = math.prod(out.shape[1:]) * out.element_size()
+        dist.all_to_all_single(ob, ib, [r * row_bytes for r in out_rows], [r * row_bytes for r in in_rows],
+                               group=self.group)
+
+    def forward(self, S, x, events=None):
+        """events: optional {"dispatch", "fc1", "combine": (start, end)} CUDA events to record."""
+        ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
+        T = x.shape[0]
+        idx, wts = ops.topk(S, self.bias, self.rs, K)
+        # one pick a "row": several picks of a token may go to the same rank, and the table builder
+        # ranks rows, so the plan runs over the expanded (token, k) sequence
+        plan = ops.tables((idx // El).to(torch.int32).reshape(-1, 1).contiguous(), W, 1)
+        send_pos = plan.exp2perm.reshape(T, K)          # [T, K] slot of each pick
+        send_counts = plan.counts[:W].to(torch.int64)   # picks to each rank
+        send = ops.pack(x, idx, send_pos, El, T * K)
+        recv_counts = torch.empty_like(send_counts)
+        self._a2a(recv_counts, send_counts, [1] * W, [1] * W)
+        sc = send_counts.tolist()
+        rc = recv_counts.tolist()
+        R_recv = sum(rc)
+        R_all = R_recv + (T if self.shared else 0)
+        stride = send.shape[1]
+        recv = torch.empty((max(R_all, 1), stride), dtype=torch.uint8, device=send.device)
+        if events:
+            events["dispatch"][0].record()
+        self._a2a(recv[:R_recv], send, rc, sc)
+        if events:
+            events["dispatch"][1].record()
+        if self.shared:
+            ops.pack_rows(x, El, recv[R_recv:R_all])
+        ids = ops.ids(recv, R_all, H)
+        tb = ops.tables(ids, El + self.shared, 128)
+        qp, sfp = ops.unpack(recv, R_all, H, tb)
+        y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, R_all, events)
+        back = torch.empty((T * K, H), dtype=y.dtype, device=y.device)
+        if events:
+            events["combine"][0].record()
+        self._a2a(back, y[:R_recv], sc, rc)
+        if events:
+            events["combine"][1].record()
+        self.last = {"received_rows": R_recv, "sent_rows": T * K, "tables": tb}
+        shared_rows = y[R_recv:R_all] if self.shared else None
+        return ops.combine(back, send_pos, wts, shared_rows, T, K, H)
+
+
+def slice_weights(w13, w13_sf, w2, w2_sf, E, shared, rank, world, H, I):
+    """This rank's experts (and the shared expert, stored last) out of full tile-major weight tensors
+    laid out as k3moe_layer_forward expects (experts back to back, the shared expert after the routed)."""
+    El = E // world
+    e0, e1 = rank * El, (rank + 1) * El
+
+    def rows(t):  # the contiguous bytes of experts [e0, e1), then the shared expert's
+        per_b = t.numel() // (E + shared)
+        parts = [t.reshape(-1)[e0 * per_b:e1 * per_b]]
+        if shared:
+            parts.append(t.reshape(-1)[E * per_b:(E + 1) * per_b])
+        return torch.cat(parts)
+
+    return {"w13": rows(w13), "w13_sf": rows(w13_sf), "w2": rows(w2), "w2_sf": rows(w2_sf)}

@@ -1,0 +1,107 @@
+"""The expert-parallel layer's steps on the CPU, made of the oracle — test
+infrastructure: with these, k3moe_ep.EPMoELayer's host logic (send plan,
+counts exchange, dispatch / combine all-to-all, receive layout) runs under
+gloo ranks on a machine without a GPU."""
+from __future__ import annotations
+
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+import oracle
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _bits(t):  # bf16 tensor -> uint16 bit array
+    return _np(t.view(torch.int16)).view(np.uint16)
+
+
+def _bf16(bits):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+
+class OracleOps:
+    def topk(self, S, bias, rs, K):
+        idx, wts = oracle.topk(_np(S), _np(bias), int(_bits(rs)[0]), K)
+        return torch.from_numpy(idx), torch.from_numpy(wts)
+
+    def tables(self, ids, E, tile):
+        tb = oracle.tables(_np(ids), E, 0, 0, tile)
+        return SimpleNamespace(counts=torch.from_numpy(tb["counts"]), exp2perm=torch.from_numpy(tb["exp2perm"]),
+                               route_map=torch.from_numpy(tb["route_map"]), cta_batch=tb["cta_batch"],
+                               cta_limit=tb["cta_limit"], meta=tb["meta"], cap_rows=tb["cap_rows"],
+                               max_ctas=tb["max_ctas"])
+
+    @staticmethod
+    def stride(H):
+        return (H + H // 32 + 4 + 15) // 16 * 16
+
+    def _rows(self, x):
+        q, sf = oracle.quant_mxfp8(_bits(x), tiled=False)
+        return q, sf
+
+    def pack(self, x, idx, send_pos, E_local, n_slots):
+        H = x.shape[1]
+        q, sf = self._rows(x)
+        buf = np.zeros((n_slots, self.stride(H)), np.uint8)
+        idx, pos = _np(idx), _np(send_pos)
+        for t in range(idx.shape[0]):
+            for k in range(idx.shape[1]):
+                p = pos[t, k]
+                buf[p, :H] = q[t]
+                buf[p, H:H + H // 32] = sf[t]
+                buf[p, H + H // 32:H + H // 32 + 4] = np.array([idx[t, k] % E_local], np.int32).view(np.uint8)
+        return torch.from_numpy(buf)
+
+    def pack_rows(self, x, eid, dst):
+        H = x.shape[1]
+        q, sf = self._rows(x)
+        d = _np(dst)
+        d[:, :H] = q
+        d[:, H:H + H // 32] = sf
+        d[:, H + H // 32:H + H // 32 + 4] = np.full((q.shape[0], 1), eid, np.int32).view(np.uint8)
+
+    def ids(self, rows, R, H):
+        r = _np(rows)[:R, H + H // 32:H + H // 32 + 4].copy()
+        return torch.from_numpy(r.view(np.int32).reshape(R, 1))
+
+    def unpack(self, rows, R, H, tb):
+        r = _np(rows)
+        perm = _np(tb.exp2perm).reshape(-1)
+        qp = np.zeros(tb.cap_rows * H, np.uint8)
+        sfp = np.zeros(tb.cap_rows * H // 32, np.uint8)
+        kg4 = H // 128
+        k = np.arange(H)
+        kb = np.arange(H // 32)
+        for i in range(R):
+            p = int(perm[i])
+            if p < 0:
+                continue
+            qp[((p // 128) * (H // 128) + k // 128) * 16384 + (p % 128) * 128 + k % 128] = r[i, :H]
+            sfp[((p // 128) * kg4 + kb // 4) * 512 + (p % 32) * 16 + ((p % 128) // 32) * 4 + kb % 4] = r[i, H:H + H // 32]
+        return qp.reshape(tb.cap_rows, H), sfp
+
+    def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None):
+        nne = int(tb.meta[0])
+        wn = {k: _np(v) for k, v in w.items()}
+        f1q, f1sf = oracle.fc1(wn["w13"], wn["w13_sf"], qp, sfp, tb.cta_batch, tb.cta_limit, 0, nne, H, I)
+        yp = oracle.fc2(wn["w2"], wn["w2_sf"], f1q, f1sf, tb.cta_batch, tb.cta_limit, 0, nne, H, I)
+        y = np.zeros((n_rows, H), np.uint16)
+        rmap = _np(tb.route_map)
+        for c in range(nne):
+            for r in range(c * 128, int(tb.cta_limit[c])):
+                y[rmap[r]] = yp[r]
+        return _bf16(y)
+
+    def combine(self, back, send_pos, wts, shared_rows, T, K, H):
+        fc2 = _bits(back)
+        meta = None
+        if shared_rows is not None:
+            fc2 = np.concatenate([fc2, _bits(shared_rows)])
+            meta = np.array([0, 0, T * K, 0], np.int32)
+        out = oracle.combine(fc2, _np(send_pos), _np(wts), meta, T, K)
+        return _bf16(out)

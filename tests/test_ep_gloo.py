@@ -1,0 +1,70 @@
+"""The expert-parallel layer's host logic on CPU: world_size 2 gloo ranks run
+k3moe_ep.EPMoELayer with oracle-built steps (tests/ep_oracle_ops.py) and the
+two halves of the output must equal, bit for bit, the single-device layer over
+all the tokens (every rank holds half the experts and its own tokens)."""
+import multiprocessing as mp
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+import cases
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+CFG = dict(T=96, H=256, I=256, E=8, K=2, shared=1, rs=2.5, seed=11)
+
+
+def _worker(rank, world, port, outdir):
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    sys.path[:0] = [here, os.path.join(root, "oracle"), os.path.join(root, "kern-k3-pp-prefill_b200")]
+    import torch
+    import torch.distributed as dist
+
+    import cases as C
+    import ep_oracle_ops
+    import k3moe_ep
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=__import__("datetime").timedelta(seconds=60))
+    c = C.make_case(**CFG)
+    T_l = c.T // world
+    rows = slice(rank * T_l, (rank + 1) * T_l)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    w = k3moe_ep.slice_weights(t(c.w13), t(c.w13_sf), t(c.w2), t(c.w2_sf), c.E, c.shared, rank, world, c.H, c.I)
+    rs = t(np.array([c.rs_bits], np.uint16)).view(torch.bfloat16)
+    layer = k3moe_ep.EPMoELayer(c.H, c.I, c.E, c.K, c.shared, w, t(c.bias), rs, ops=ep_oracle_ops.OracleOps())
+    out = layer.forward(t(c.S[rows]), t(c.x_bits[rows]).view(torch.bfloat16))
+    np.save(os.path.join(outdir, f"out{rank}.npy"), out.view(torch.int16).numpy().view(np.uint16))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep2_gloo_matches_single_device():
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(180)
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        got = np.concatenate([np.load(os.path.join(d, f"out{r}.npy")) for r in range(2)])
+    c = cases.make_case(**CFG)
+    ref, _ = cases.oracle_forward(c)
+    assert np.array_equal(got, ref)

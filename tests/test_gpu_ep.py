@@ -1,0 +1,94 @@
+"""Expert parallelism on 2 GPUs over NCCL: every rank holds half the experts
+and its own tokens; the layer's output must equal, bit for bit, the single-GPU
+layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs."""
+import multiprocessing as mp
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(T_local=160, H=1024, I=512, E=16, K=4, shared=1, rs=2.5)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, outdir):
+    import datetime
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    sys.path[:0] = [here, os.path.join(root, "kern-k3-pp-prefill_b200")]
+    import torch
+    import torch.distributed as dist
+
+    import k3moe
+    import k3moe_ep
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    c = CFG
+    H, I, E, K, sh = c["H"], c["I"], c["E"], c["K"], c["shared"]
+    T = c["T_local"] * world
+    w13, w13_sf = k3moe.synth_mxfp4(21, (E + sh) * 2 * I, H, 0.02, device=dev)
+    w2, w2_sf = k3moe.synth_mxfp4(22, (E + sh) * H, I, 0.02, device=dev)
+    # inputs made on the host, so every rank and the one-GPU reference see the same bytes
+    import numpy as np
+
+    rng = np.random.default_rng(5)
+    xf = rng.standard_normal((T, H)).astype(np.float32)
+    x = torch.from_numpy(xf).to(torch.bfloat16).to(dev)
+    S = torch.from_numpy((x.float().cpu().numpy().astype(np.float64) @ (rng.standard_normal((H, E)) / H ** 0.5))
+                         .astype(np.float32)).to(dev)
+    bias = torch.from_numpy(rng.uniform(-0.1, 0.1, E).astype(np.float32)).to(dev)
+    rs = torch.tensor([c["rs"]], dtype=torch.bfloat16, device=dev)
+    rows = slice(rank * c["T_local"], (rank + 1) * c["T_local"])
+    w = k3moe_ep.slice_weights(w13, w13_sf, w2, w2_sf, E, sh, rank, world, H, I)
+    layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev)
+    outs = [layer.forward(S[rows].contiguous(), x[rows].contiguous()) for _ in range(2)]  # twice: reused buffers
+    full = [torch.empty_like(outs[1]) for _ in range(world)]
+    dist.all_gather(full, outs[1])
+    torch.cuda.synchronize()
+    ok = torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    if rank == 0:
+        ref = k3moe.MoELayer(H, I, E, K, sh, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
+        want = ref.forward(S, x)
+        got = torch.cat(full)
+        torch.cuda.synchronize()
+        same = got.view(torch.int16) == want.view(torch.int16)
+        bad_rows = (~same.all(1)).nonzero().flatten().tolist()
+        diff = (got.float() - want.float()).abs().max().item()
+        ok = ok and not bad_rows
+        open(os.path.join(outdir, "result"), "w").write(
+            "ok" if ok else f"mismatch: repeat-equal={ok} rows={bad_rows[:20]} n={len(bad_rows)} maxdiff={diff}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep2_nccl_bit_identical_to_one_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs (run with gpurun --gpus 2)")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert open(os.path.join(d, "result")).read() == "ok"
