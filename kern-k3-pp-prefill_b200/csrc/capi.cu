@@ -10,6 +10,7 @@
 #include "gemm.cu"
 #include "route.cu"
 #include "ep.cu"
+#include "dropin.cu"
 
 using namespace k3;
 

@@ -1,0 +1,5 @@
+// The drop-in kernel module (a cubin a manifest binds by entry name, like the
+// reference's source/*.cu modules): the route.cu kernels the entries build on
+// and the extern "C" entries of dropin.cu, with no host code.
+#include "route.cu"
+#include "dropin.cu"

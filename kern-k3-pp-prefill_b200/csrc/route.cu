@@ -331,12 +331,11 @@ __global__ void __launch_bounds__(256) quant_tiled_kernel(const bf16* __restrict
 // out[t] = bf16( sum_{k=0..K-1, p>=0} fma(w[t,k], fc2[p], acc)  (+ fc2[shared_base+t]) ),
 // f32, k in order, the shared expert (weight 1) last.  Rows t >= T are zero.
 // One block a row, 8 columns a thread a step.
-__global__ void __launch_bounds__(256) combine_kernel(const bf16* __restrict__ fc2, const int* __restrict__ exp2perm,
-                                                      const float* __restrict__ wts, const int* __restrict__ meta,
-                                                      bf16* __restrict__ out, int ldo, int T, int K, int cols) {
+__device__ __forceinline__ void combine_row(const bf16* __restrict__ fc2, const int* __restrict__ exp2perm,
+                                            const float* __restrict__ wts, const int* __restrict__ meta,
+                                            bf16* __restrict__ out, int ldo, int T, int K, int cols, int t) {
   __shared__ int sp[17];
   __shared__ float sw[17];
-  const int t = blockIdx.x;
   const int shared_base = meta ? meta[2] : -1;
   int n = 0;
   if (t < T) {
@@ -373,6 +372,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const bf16* __restrict__ f
     o.w = f2_to_bf16x2(acc[6], acc[7]);
     reinterpret_cast<uint4*>(out + (long long)t * ldo)[h] = o;
   }
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(const bf16* __restrict__ fc2, const int* __restrict__ exp2perm,
+                                                      const float* __restrict__ wts, const int* __restrict__ meta,
+                                                      bf16* __restrict__ out, int ldo, int T, int K, int cols) {
+  combine_row(fc2, exp2perm, wts, meta, out, ldo, T, K, cols, blockIdx.x);
 }
 
 // ============================================================ MXFP4 weights

@@ -24,10 +24,28 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
+CUBIN = os.path.join(HERE, "k3moe_module.cubin")
+
+
+def build_cubin(nvcc: str) -> str:
+    """The drop-in kernel module (csrc/module.cu: the extern "C" entries with the reference's names)."""
+    cmd = [nvcc, "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
+           os.path.join(HERE, "csrc", "module.cu"), "-o", CUBIN + ".tmp"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("nvcc failed for k3moe_module.cubin")
+    os.replace(CUBIN + ".tmp", CUBIN)
+    return CUBIN
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return OUT
     nvcc = os.environ.get("NVCC", "nvcc")
+    if not force and up_to_date():
+        if not os.path.exists(CUBIN) or os.path.getmtime(CUBIN) < os.path.getmtime(OUT):
+            build_cubin(nvcc)
+        return OUT
+    build_cubin(nvcc)
     cmd = [nvcc, *NVCC_FLAGS, SRC, "-o", OUT + ".tmp"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -31,12 +31,14 @@ def available(module: str) -> bool:
 
 
 def function(module: str, entry: str):
+    """`module`: a cubin name under oracle/_ref, or a path ending in .cubin."""
     torch.cuda.init()
     torch.zeros(1, device="cuda")  # the primary context is current
     d = _drv()
     if module not in _modules:
         m = ctypes.c_void_p()
-        rc = d.cuModuleLoad(ctypes.byref(m), os.path.join(REF_DIR, module + ".cubin").encode())
+        path = module if module.endswith(".cubin") else os.path.join(REF_DIR, module + ".cubin")
+        rc = d.cuModuleLoad(ctypes.byref(m), path.encode())
         if rc != 0:
             raise RuntimeError(f"cuModuleLoad({module}) = {rc}")
         _modules[module] = m

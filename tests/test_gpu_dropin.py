@@ -1,0 +1,156 @@
+"""The drop-in module (kern-k3-pp-prefill_b200/k3moe_module.cubin): each entry,
+bound by name and launched with the reference manifest's geometry, against the
+same entry of the reference's module built from source (oracle/_ref), on the
+same inputs into output buffers poisoned the same way: byte equality."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import refkern as rk
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+MOD = os.path.join(ROOT, "kern-k3-pp-prefill_b200", "k3moe_module.cubin")
+TOPK, E, LATENT = 16, 896, 3584
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _poison(shape, dtype, dev):
+    t = torch.empty(shape, dtype=dtype, device=dev)
+    t.view(torch.uint8).fill_(0x5A)
+    return t
+
+
+def _both(ref_module, entry, grid, block, make_args):
+    """Launch the reference entry and ours on argument sets built by make_args(); return both sets."""
+    ra, oa = make_args(), make_args()
+    rk.launch(rk.function(ref_module, entry), grid, block, ra[0])
+    rk.launch(rk.function(MOD, entry), grid, block, oa[0])
+    torch.cuda.synchronize()
+    return ra[1], oa[1]
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 3584), (333, 7168), (8192, 3584)])
+def test_moe_quant(dev, rows, cols):
+    rng = np.random.default_rng(rows)
+    x = _t(oracle.bf16_bits((rng.standard_normal((rows, cols)) * np.exp(rng.uniform(-5, 5, (rows, 1))))
+                            .astype(np.float32)), dev).view(torch.bfloat16)
+
+    def mk():
+        q, sf = _poison((rows, cols), torch.uint8, dev), _poison((rows, cols // 32), torch.uint8, dev)
+        return [rk.P(x), rk.P(q), rk.P(sf), rk.I(rows), rk.I(cols)], (q, sf)
+
+    (rq, rsf), (q, sf) = _both("k3_moe_prefill", "kern_k3_moe_quant", (-(-rows * cols // 32 // 256), 1, 1),
+                               (256, 1, 1), mk)
+    assert torch.equal(q, rq) and torch.equal(sf, rsf)
+
+
+@pytest.mark.parametrize("rows,cols", [(130, 3584), (1000, 7168)])
+def test_mxfp8_quant(dev, rows, cols):
+    rng = np.random.default_rng(cols + rows)
+    x = _t(oracle.bf16_bits(rng.standard_normal((rows, cols)).astype(np.float32)), dev).view(torch.bfloat16)
+    nsf = -(-rows // 128) * -(-cols // 128) * 512
+
+    def mk():
+        q, sf = _poison((rows, cols), torch.uint8, dev), _poison(nsf, torch.uint8, dev)
+        return [rk.P(x), rk.I(cols), rk.P(q), rk.P(sf), rk.I(rows), rk.I(cols)], (q, sf)
+
+    (rq, rsf), (q, sf) = _both("k3_mxfp8", "kern_k3_mxfp8_quant", (148, 1, 1), (256, 1, 1), mk)
+    assert torch.equal(q, rq) and torch.equal(sf, rsf)
+
+
+@pytest.mark.parametrize("B", [1, 7, 64, 2048])
+def test_router_topk(dev, B):
+    rng = np.random.default_rng(B + 3)
+    S = _t((rng.standard_normal((B, E)) * 2).astype(np.float32), dev)
+    bias = _t((rng.standard_normal(E) * 0.1).astype(np.float32), dev)
+    rs = _t(oracle.bf16_bits(np.array([2.5], np.float32)), dev).view(torch.bfloat16)
+
+    def mk():
+        idx, w = _poison((B, TOPK), torch.int32, dev), _poison((B, TOPK), torch.float32, dev)
+        return [rk.P(S), rk.P(bias), rk.P(rs), rk.P(idx), rk.P(w), rk.I(B)], (idx, w)
+
+    (ri, rw), (i, w) = _both("k3_prefill_glue", "kern_k3g_router_topk", (-(-B // 4), 1, 1), (128, 1, 1), mk)
+    assert torch.equal(i, ri) and torch.equal(w.view(torch.int32), rw.view(torch.int32))
+
+
+@pytest.mark.parametrize("T,El,rank,tile", [(48, 56, 3, 128), (4096, 64, 5, 64), (1, 16, 0, 128)])
+def test_route_count_tables_scatter(dev, T, El, rank, tile):
+    rng = np.random.default_rng(T + El)
+    ids_np = np.stack([rng.choice(E, TOPK, replace=False) for _ in range(T)]).astype(np.int32)
+    for t in range(0, T, 3):
+        ids_np[t] = rank * El + rng.choice(El, TOPK, replace=False)
+    ids = _t(ids_np, dev)
+    blocks = -(-T // 256)
+    ctas = El + -(-T * TOPK // tile)
+    outs = {}
+    for name, mod in (("ref", "k3_moe_prefill"), ("ours", MOD)):
+        bc = _poison(blocks * El, torch.int32, dev)
+        bo = _poison(blocks * El, torch.int32, dev)
+        cb, cl = _poison(ctas, torch.int32, dev), _poison(ctas, torch.int32, dev)
+        nne, tp = _poison(1, torch.int32, dev), _poison(1, torch.int32, dev)
+        rmap, e2p = _poison(ctas * tile, torch.int32, dev), _poison((T, TOPK), torch.int32, dev)
+        rk.launch(rk.function(mod, "kern_k3_moe_route_count"), (blocks, 1, 1), (256, 1, 1),
+                  [rk.P(ids), rk.I(T), rk.I(rank), rk.I(El), rk.P(bc)])
+        rk.launch(rk.function(mod, "kern_k3_moe_route_tables"), (1, 1, 1), (1024, 1, 1),
+                  [rk.P(bc), rk.I(blocks), rk.I(El), rk.I(tile), rk.P(bo), rk.P(cb), rk.P(cl), rk.P(nne), rk.P(tp),
+                   rk.P(rmap)])
+        rk.launch(rk.function(mod, "kern_k3_moe_route_scatter"), (blocks, 1, 1), (256, 1, 1),
+                  [rk.P(ids), rk.P(bo), rk.I(T), rk.I(rank), rk.I(El), rk.P(rmap), rk.P(e2p)])
+        torch.cuda.synchronize()
+        outs[name] = [bc, bo, cb, cl, nne, tp, rmap, e2p]
+    for a, b in zip(outs["ref"], outs["ours"]):
+        assert torch.equal(a, b)
+
+
+def _fc2_inputs(T, cols, dev, seed):
+    rng = np.random.default_rng(seed)
+    idx = np.stack([rng.choice(E, TOPK, replace=False) for _ in range(T)]).astype(np.int32)
+    e2p = np.where(idx % 3 == 0, -1, np.arange(T * TOPK).reshape(T, TOPK)).astype(np.int32)  # some foreign picks
+    fc2 = oracle.bf16_bits(rng.standard_normal((T * TOPK, cols)).astype(np.float32))
+    wts = rng.uniform(0, 0.3, (T, TOPK)).astype(np.float32)
+    gamma = oracle.bf16_bits(rng.uniform(0.5, 1.5, cols).astype(np.float32))
+    return (_t(fc2, dev).view(torch.bfloat16), _t(e2p, dev), _t(wts, dev),
+            _t(gamma, dev).view(torch.bfloat16))
+
+
+@pytest.mark.parametrize("T,rows,cols", [(37, 64, 3584), (300, 300, 7168)])
+def test_finalize(dev, T, rows, cols):
+    fc2, e2p, wts, _ = _fc2_inputs(T, cols, dev, T)
+
+    def mk():
+        out = _poison((rows, cols), torch.bfloat16, dev)
+        return [rk.P(fc2), rk.P(e2p), rk.P(wts), rk.P(out), rk.I(T), rk.I(cols)], out
+
+    ro, o = _both("k3_moe_prefill", "kern_k3_moe_finalize", (rows, 1, 1), (cols // 8, 1, 1), mk)
+    assert torch.equal(o.view(torch.int16), ro.view(torch.int16))
+
+
+@pytest.mark.parametrize("T,rows", [(5, 8), (512, 512)])
+def test_finalize_rms(dev, T, rows):
+    cols = LATENT
+    fc2, e2p, wts, gamma = _fc2_inputs(T, cols, dev, T + 1)
+
+    def mk_glue():
+        out = _poison((rows, cols), torch.bfloat16, dev)
+        return [rk.P(fc2), rk.P(e2p), rk.P(wts), rk.P(gamma), rk.P(out), rk.I(T), rk.I(cols)], out
+
+    ro, o = _both("k3_prefill_glue", "kern_k3g_finalize_rms", (rows, 1, 1), (cols // 8, 1, 1), mk_glue)
+    assert torch.equal(o.view(torch.int16), ro.view(torch.int16))
+    # the route module's variant writes the first LATENT columns of ldo-wide rows (only that entry of the
+    # module runs here; its grid-barrier router entry is not launched)
+    ldo = cols + 256
+
+    def mk_route():
+        out = _poison((rows, ldo), torch.bfloat16, dev)
+        return [rk.P(fc2), rk.P(e2p), rk.P(wts), rk.P(gamma), rk.P(out), rk.I(ldo), rk.I(T)], out
+
+    ro, o = _both("k3_moe_route", "kern_k3g_moe_finalize_rms", (rows, 1, 1), (cols // 8, 1, 1), mk_route)
+    assert torch.equal(o.view(torch.int16), ro.view(torch.int16))
