@@ -138,6 +138,16 @@ int k3moe_fc2(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, con
               const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, void* fc2_bf16, int H, int I,
               int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream);
 
+/* FC1 with the gate chosen: K3MOE_ACT_SWIGLU h = silu(g) * u (k3moe_fc1), or
+ * K3MOE_ACT_SITU, K3's h = 4 tanh(g/4) sigmoid(g) * 25 tanh(u/25)
+ * (docs/k3-kernel-abi.md:73; harness/k3/ref.h:97-101; the FC1 cubin's
+ * siTuGlu with alpha 4, beta 25: scripts/k3_moe_bmm.py:16-20). */
+enum { K3MOE_ACT_SWIGLU = 0, K3MOE_ACT_SITU = 1 };
+int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
+                  const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* fc1_q,
+                  uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
+                  int activation, k3moe_stream_t stream);
+
 /* FC2 storing permuted row r at row out_rows[r] of fc2_bf16 (the expert-parallel
  * layer passes route_map, so rows come out in the order they were received). */
 int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
@@ -205,6 +215,7 @@ typedef struct k3moe_layer_args {
   const uint8_t* w2;  const uint8_t* w2_sf;   /* [E + shared, H, I/2] */
   void* out;          /* bf16 [T, ldo] */
   int ldo;
+  int activation;     /* FC1 gate: K3MOE_ACT_SWIGLU (0) or K3MOE_ACT_SITU (1) */
 } k3moe_layer_args;
 
 size_t k3moe_layer_workspace_size(int T, int H, int I, int E, int K, int shared);

@@ -100,7 +100,8 @@ void launch_topk(const float* S, int lds, const float* bias, const bf16* rs, int
 int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* act, const uint8_t* act_sf,
                 const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* out_q,
                 uint8_t* out_sf, void* out_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas,
-                uint32_t* err, cudaStream_t stream, const int32_t* out_rows = nullptr) {
+                uint32_t* err, cudaStream_t stream, const int32_t* out_rows = nullptr, int activation = 0) {
+  if (activation != 0 && activation != 1) return K3MOE_EINVAL;
   if (H <= 0 || I <= 0 || H % 256 || I % 256 || n_experts <= 0 || cap_rows <= 0 || cap_rows % 128 || max_ctas <= 0 ||
       (long long)max_ctas * 128 > cap_rows)
     return K3MOE_EINVAL;
@@ -121,6 +122,7 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   p.out_sf = out_sf;
   p.out_bf16 = reinterpret_cast<bf16*>(out_bf16);
   p.out_rows = out_rows;
+  p.act = activation;
   p.err = err;
   p.K = K;
   p.rows_per_expert = rows_per_expert;
@@ -268,6 +270,14 @@ int k3moe_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, 
                      n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
+                  const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* fc1_q,
+                  uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
+                  int activation, k3moe_stream_t stream) {
+  return gemm_launch(MODE_FC1, w13, w13_sf, q_perm, sf_perm, cta_batch, cta_limit, meta, fc1_q, fc1_sf, nullptr, H, I,
+                     n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream), nullptr, activation);
+}
+
 int k3moe_fc2(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
               const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, void* fc2_bf16, int H, int I,
               int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream) {
@@ -348,8 +358,8 @@ int k3moe_layer_forward_events(const k3moe_layer_args* a, void* workspace, size_
   if (rc) return rc;
   mark(3);
   const int nexp = a->E + shared;
-  rc = k3moe_fc1(a->w13, a->w13_sf, U8(L_QP), U8(L_SFP), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META), U8(L_FC1Q),
-                 U8(L_FC1SF), a->H, a->I, nexp, L.cap_rows, L.max_ctas, err, stream);
+  rc = k3moe_fc1_act(a->w13, a->w13_sf, U8(L_QP), U8(L_SFP), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META),
+                     U8(L_FC1Q), U8(L_FC1SF), a->H, a->I, nexp, L.cap_rows, L.max_ctas, err, a->activation, stream);
   if (rc) return rc;
   mark(4);
   rc = k3moe_fc2(a->w2, a->w2_sf, U8(L_FC1Q), U8(L_FC1SF), I32(L_CTA_BATCH), I32(L_CTA_LIMIT), I32(L_META),

@@ -78,7 +78,15 @@ struct GemmParams {
   int cap_rows;             // permuted-row capacity of the activations and the outputs
   int max_ctas;             // capacity of the CTA tables
   unsigned long long* trace;  // optional per-role cycle counters (16 a mode), or null
+  int act;                  // FC1 gate: 0 SwiGLU silu(g)*u, 1 K3's SiTU 4 tanh(g/4) sigmoid(g) * 25 tanh(u/25)
 };
+
+// FC1's gated activation of (gate g, up u)
+__device__ __forceinline__ float gated_act(float g, float u, int act) {
+  const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
+  if (act == 0) return g * sg * u;
+  return 4.0f * tanhf(0.25f * g) * sg * (25.0f * tanhf(0.04f * u));
+}
 
 struct Unit {
   int valid, e, row0, n, fb;
@@ -334,7 +342,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             for (int j = 0; j < 32; ++j) {
               const float gf = __uint_as_float(v[g][j]);
               const float uf = __uint_as_float(v[2 + g][j]);
-              hv[j] = __fdividef(gf, 1.0f + __expf(-gf)) * uf;
+              hv[j] = gated_act(gf, uf, p.act);
               amax = fmaxf(amax, fabsf(hv[j]));
             }
             const int e = mx8_exponent_exact(amax);

@@ -52,6 +52,7 @@ SIGNATURES = {
     "k3moe_set_trace": (_I, [_P]),
     "k3moe_route_tables_noalloc": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "k3moe_fc2_to_rows": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "k3moe_fc1_act": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P]),
     "k3moe_ep_row_stride": (_I, [_I]),
     "k3moe_ep_pack": (_I, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _P]),
     "k3moe_ep_ids": (_I, [_P, _I, _I, _I, _P, _P]),
@@ -113,7 +114,11 @@ class k3moe_layer_args(ctypes.Structure):
         ("w13", ctypes.c_void_p), ("w13_sf", ctypes.c_void_p),
         ("w2", ctypes.c_void_p), ("w2_sf", ctypes.c_void_p),
         ("out", ctypes.c_void_p), ("ldo", ctypes.c_int),
+        ("activation", ctypes.c_int),
     ]
+
+
+ACT_SWIGLU, ACT_SITU = 0, 1
 
 
 # ------------------------------------------------------------------ steps
@@ -209,13 +214,14 @@ def quant_permute(x: torch.Tensor, tables: Tables, stream=None):
     return qp, sfp
 
 
-def fc1(w13, w13_sf, qp, sfp, tables: Tables, H: int, I: int, n_experts: int, err: torch.Tensor, stream=None):
+def fc1(w13, w13_sf, qp, sfp, tables: Tables, H: int, I: int, n_experts: int, err: torch.Tensor, stream=None,
+        activation: int = ACT_SWIGLU):
     cap = tables.cap_rows
     out_q = torch.zeros((cap, I), dtype=torch.uint8, device=qp.device)
     out_sf = torch.zeros(cap * I // 32, dtype=torch.uint8, device=qp.device)
-    _check(lib().k3moe_fc1(_p(w13), _p(w13_sf), _p(qp), _p(sfp), _p(tables.cta_batch), _p(tables.cta_limit),
-                           _p(tables.meta), _p(out_q), _p(out_sf), H, I, n_experts, cap, tables.max_ctas, _p(err),
-                           _stream(stream)), "fc1")
+    _check(lib().k3moe_fc1_act(_p(w13), _p(w13_sf), _p(qp), _p(sfp), _p(tables.cta_batch), _p(tables.cta_limit),
+                               _p(tables.meta), _p(out_q), _p(out_sf), H, I, n_experts, cap, tables.max_ctas, _p(err),
+                               activation, _stream(stream)), "fc1")
     return out_q, out_sf
 
 
@@ -274,11 +280,13 @@ class MoELayer:
 
     Weights: w13 [E+shared, 2I, H/2] packed E2M1 ([gate; up] rows), w2 [E+shared, H, I/2],
     scales tiled over the flattened rows.  forward() runs top-k -> tables -> MXFP8 permute ->
-    FC1 (SwiGLU, MXFP8) -> FC2 -> combine through k3moe_layer_forward.
+    FC1 (SwiGLU or K3's SiTU, MXFP8) -> FC2 -> combine through k3moe_layer_forward.
     """
 
-    def __init__(self, H, I, E, K, shared, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens, device="cuda"):
+    def __init__(self, H, I, E, K, shared, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens, device="cuda",
+                 activation=ACT_SWIGLU):
         self.H, self.I, self.E, self.K, self.shared = H, I, E, K, int(shared)
+        self.activation = activation
         self.w13, self.w13_sf, self.w2, self.w2_sf = w13, w13_sf, w2, w2_sf
         self.bias, self.rs = bias, rs
         self.max_tokens = max_tokens
@@ -297,6 +305,7 @@ class MoELayer:
         a.w13, a.w13_sf, a.w2, a.w2_sf = (self.w13.data_ptr(), self.w13_sf.data_ptr(), self.w2.data_ptr(),
                                           self.w2_sf.data_ptr())
         a.out, a.ldo = out.data_ptr(), out.stride(0)
+        a.activation = self.activation
         return a
 
     def forward(self, S, x, out=None, stream=None):

@@ -61,6 +61,10 @@ void orc_combine(const uint16_t* fc2, const int32_t* exp2perm, const float* wts,
 void orc_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
              const int32_t* cta_batch, const int32_t* cta_limit, int c0, int c1, int H, int I, uint8_t* fc1_q,
              uint8_t* fc1_sf);
+/* act: 0 SwiGLU, 1 K3's SiTU (harness/k3/ref.h:97-101) */
+void orc_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
+                 const int32_t* cta_batch, const int32_t* cta_limit, int c0, int c1, int H, int I, uint8_t* fc1_q,
+                 uint8_t* fc1_sf, int act);
 void orc_fc2(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
              const int32_t* cta_batch, const int32_t* cta_limit, int c0, int c1, int H, int I, uint16_t* fc2);
 

@@ -48,17 +48,31 @@ static float dot(const float* a, const float* b, int n) {
   return s;
 }
 
-/* Every tile c in [c0, c1): expert e = cta_batch[c], rows [128c, cta_limit[c]). */
+/* the gate: 0 SwiGLU silu(g) * u; 1 K3's SiTU 4 tanh(g/4) sigmoid(g) * 25 tanh(u/25)
+ * (harness/k3/ref.h:97-101), in double */
+static float gated_act(float g, float u, int act) {
+  const double gd = g, ud = u, sg = 1.0 / (1.0 + exp(-gd));
+  if (act == 0) return (float)(gd * sg * ud);
+  return (float)(4.0 * tanh(gd / 4.0) * sg * 25.0 * tanh(ud / 25.0));
+}
+
 void orc_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
              const int32_t* cta_batch, const int32_t* cta_limit, int c0, int c1, int H, int I, uint8_t* fc1_q,
              uint8_t* fc1_sf) {
+  orc_fc1_act(w13, w13_sf, q_perm, sf_perm, cta_batch, cta_limit, c0, c1, H, I, fc1_q, fc1_sf, 0);
+}
+
+/* Every tile c in [c0, c1): expert e = cta_batch[c], rows [128c, cta_limit[c]). */
+void orc_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
+                 const int32_t* cta_batch, const int32_t* cta_limit, int c0, int c1, int H, int I, uint8_t* fc1_q,
+                 uint8_t* fc1_sf, int act) {
   const int kg4_out = (I / 32 + 3) / 4;
   for (int c = c0; c < c1; ++c) {
     const int e = cta_batch[c], row0 = c * 128, n = cta_limit[c] - row0;
     if (n <= 0) continue;
-    float* act = (float*)malloc(sizeof(float) * (size_t)n * H);
+    float* xa = (float*)malloc(sizeof(float) * (size_t)n * H);
     float* h = (float*)malloc(sizeof(float) * (size_t)n * I);
-    for (int j = 0; j < n; ++j) dequant_a_row(q_perm, sf_perm, row0 + j, H, act + (size_t)j * H);
+    for (int j = 0; j < n; ++j) dequant_a_row(q_perm, sf_perm, row0 + j, H, xa + (size_t)j * H);
 #pragma omp parallel
     {
       float* wg = (float*)malloc(sizeof(float) * H);
@@ -68,9 +82,9 @@ void orc_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, c
         dequant_w_row(w13, w13_sf, (long long)e * 2 * I + f, H, wg);
         dequant_w_row(w13, w13_sf, (long long)e * 2 * I + I + f, H, wu);
         for (int j = 0; j < n; ++j) {
-          const float g = dot(wg, act + (size_t)j * H, H);
-          const float u = dot(wu, act + (size_t)j * H, H);
-          h[(size_t)j * I + f] = g / (1.0f + expf(-g)) * u;
+          const float g = dot(wg, xa + (size_t)j * H, H);
+          const float u = dot(wu, xa + (size_t)j * H, H);
+          h[(size_t)j * I + f] = gated_act(g, u, act);
         }
       }
       free(wg);
@@ -89,7 +103,7 @@ void orc_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, c
         for (int i = 0; i < 32; ++i) grp[i] = orc_f32_to_e4m3_sat(h[(size_t)j * I + kb * 32 + i] * s);
         fc1_sf[orc_sf_tiled_offset(row0 + j, kb, kg4_out)] = (uint8_t)(ex + 127);
       }
-    free(act);
+    free(xa);
     free(h);
   }
 }

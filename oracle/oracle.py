@@ -140,12 +140,13 @@ def combine(fc2_bits, exp2perm, wts, meta, T, K, out_rows=None):
     return out
 
 
-def fc1(w13, w13_sf, qp, sfp, cta_batch, cta_limit, c0, c1, H, I, out_q=None, out_sf=None):
+def fc1(w13, w13_sf, qp, sfp, cta_batch, cta_limit, c0, c1, H, I, out_q=None, out_sf=None, act=0):
+    """act: 0 SwiGLU, 1 K3's SiTU."""
     cap = qp.shape[0]
     out_q = np.zeros((cap, I), np.uint8) if out_q is None else out_q
     out_sf = np.zeros(cap * I // 32, np.uint8) if out_sf is None else out_sf
-    lib().orc_fc1(_p(w13), _p(w13_sf), _p(qp), _p(sfp), _p(np.ascontiguousarray(cta_batch, np.int32)),
-                  _p(np.ascontiguousarray(cta_limit, np.int32)), c0, c1, H, I, _p(out_q), _p(out_sf))
+    lib().orc_fc1_act(_p(w13), _p(w13_sf), _p(qp), _p(sfp), _p(np.ascontiguousarray(cta_batch, np.int32)),
+                      _p(np.ascontiguousarray(cta_limit, np.int32)), c0, c1, H, I, _p(out_q), _p(out_sf), act)
     return out_q, out_sf
 
 
@@ -188,14 +189,14 @@ def dequant_rows(q: np.ndarray, sf_tiled: np.ndarray, rows: np.ndarray) -> np.nd
     return (v * s[:, :, None]).reshape(len(rows), cols)
 
 
-def moe_forward(S, bias, rs_bits, x_bits, w13, w13_sf, w2, w2_sf, E, K, H, I, shared):
+def moe_forward(S, bias, rs_bits, x_bits, w13, w13_sf, w2, w2_sf, E, K, H, I, shared, act=0):
     """The whole layer on the CPU (small configs): returns (out bf16 bits, intermediates)."""
     T = x_bits.shape[0]
     idx, wts = topk(S, bias, rs_bits, K)
     tb = tables(idx, E, 0, shared)
     qp, sfp = quant_permute(x_bits, tb["exp2perm"], tb["meta"], tb["cap_rows"])
     nne = int(tb["meta"][0])
-    f1q, f1sf = fc1(w13, w13_sf, qp, sfp, tb["cta_batch"], tb["cta_limit"], 0, nne, H, I)
+    f1q, f1sf = fc1(w13, w13_sf, qp, sfp, tb["cta_batch"], tb["cta_limit"], 0, nne, H, I, act=act)
     y = fc2(w2, w2_sf, f1q, f1sf, tb["cta_batch"], tb["cta_limit"], 0, nne, H, I)
     out = combine(y, tb["exp2perm"], wts, tb["meta"], T, K)
     return out, dict(idx=idx, wts=wts, tables=tb, q_perm=qp, sf_perm=sfp, fc1_q=f1q, fc1_sf=f1sf, fc2=y)

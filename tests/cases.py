@@ -59,9 +59,9 @@ def make_case(T, H, I, E, K, shared=0, rs=1.0, seed=0, wsd=0.02, bias=None) -> C
     return Case(T, H, I, E, K, shared, S, b, rs_bits, x_bits, w13, w13_sf, w2, w2_sf)
 
 
-def oracle_forward(c: Case):
+def oracle_forward(c: Case, act: int = 0):
     return oracle.moe_forward(c.S, c.bias, c.rs_bits, c.x_bits, c.w13, c.w13_sf, c.w2, c.w2_sf, c.E, c.K, c.H, c.I,
-                              c.shared)
+                              c.shared, act)
 
 
 def to_device(c: Case, dev):

@@ -93,6 +93,22 @@ def test_layer_against_oracle(dev, cfg):
     assert np.array_equal(e2p, inter["tables"]["exp2perm"])
 
 
+@pytest.mark.parametrize("cfg", [dict(T=200, H=1024, I=512, E=16, K=4, shared=1, rs=1.0),
+                                 dict(T=64, H=3584, I=3072, E=64, K=16, shared=0, rs=2.5)])
+def test_layer_situ_against_oracle(dev, cfg):
+    # K3's own gate (the reference FC1's siTuGlu, alpha 4 / beta 25), at the native latent shape too
+    c = cases.make_case(**cfg, seed=9)
+    ref_out, _ = cases.oracle_forward(c, act=1)
+    g = cases.to_device(c, dev)
+    layer = k3moe.MoELayer(c.H, c.I, c.E, c.K, c.shared, g["w13"], g["w13_sf"], g["w2"], g["w2_sf"], g["bias"],
+                           g["rs"], max_tokens=c.T, device=dev, activation=k3moe.ACT_SITU)
+    out = layer.forward(g["S"], g["x"])
+    torch.cuda.synchronize()
+    layer.check_device_error(c.T)
+    ok, rel, ratio = cases.within_contract(out.float().cpu().numpy(), oracle.bf16_to_f32(ref_out))
+    assert ok, f"SiTU layer rel-L2 {rel:.3e}, worst element at {ratio:.2f}x its bound"
+
+
 def test_layer_repeatable(dev):
     c = cases.make_case(T=256, H=1024, I=512, E=16, K=4, shared=1, rs=2.5, seed=3)
     g = cases.to_device(c, dev)
