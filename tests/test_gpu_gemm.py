@@ -68,6 +68,44 @@ def test_fc1_fc2_against_oracle(dev, cfg):
     assert ok, f"fc2 rel-L2 {rel:.3e}, worst element at {ratio:.2f}x its bound"
 
 
+@pytest.mark.parametrize("shared", [0, 1])
+def test_fc1_fc2_tile_shapes(dev, shared):
+    # ragged experts: 1 row, 16-row and 32-row boundaries, one short of and one past a full tile, an empty
+    # expert, and experts spanning two tiles; one pick a token (K = 1) so the histogram is exact
+    counts = [1, 15, 16, 17, 95, 96, 97, 128, 129, 0, 200, 33, 64, 80]
+    E = len(counts)
+    idx = np.concatenate([np.full(n, e, np.int32) for e, n in enumerate(counts)]).reshape(-1, 1)
+    idx = idx[np.random.default_rng(5).permutation(len(idx))]
+    T = len(idx)
+    c = cases.make_case(T=T, H=512, I=256, E=E, K=1, shared=shared, seed=4)
+    tb = oracle.tables(idx, E, 0, shared)
+    qp, sfp = oracle.quant_permute(c.x_bits, tb["exp2perm"], tb["meta"], tb["cap_rows"])
+    t = k3moe.route_tables(_t(idx, dev), E, 0, shared)
+    g = cases.to_device(c, dev)
+    err = torch.zeros(4, dtype=torch.int32, device=dev)
+    ne = E + shared
+    f1q, f1sf = k3moe.fc1(g["w13"], g["w13_sf"], _t(qp, dev), _t(sfp, dev), t, c.H, c.I, ne, err)
+    y = k3moe.fc2(g["w2"], g["w2_sf"], f1q, f1sf, t, c.H, c.I, ne, err)
+    torch.cuda.synchronize()
+    assert err.cpu().numpy()[:2].tolist() == [0, 0]
+    nne = int(tb["meta"][0])
+    rows = _rows_of(tb)
+    ref_q, ref_sf = oracle.fc1(c.w13, c.w13_sf, qp, sfp, tb["cta_batch"], tb["cta_limit"], 0, nne, c.H, c.I)
+    got = oracle.dequant_rows(f1q.cpu().numpy(), f1sf.cpu().numpy(), rows)
+    ref = oracle.dequant_rows(ref_q, ref_sf, rows)
+    assert cases.rel_l2(got, ref) <= 2e-2
+    # per tile, so a wrong tile shows which size broke
+    for cidx in range(nne):
+        r = np.arange(cidx * 128, int(tb["cta_limit"][cidx]))
+        rel = cases.rel_l2(oracle.dequant_rows(f1q.cpu().numpy(), f1sf.cpu().numpy(), r),
+                           oracle.dequant_rows(ref_q, ref_sf, r))
+        assert rel <= 2e-2, f"fc1 tile {cidx} ({len(r)} rows) rel-L2 {rel:.3e}"
+    ref_y = oracle.fc2(c.w2, c.w2_sf, f1q.cpu().numpy(), f1sf.cpu().numpy(), tb["cta_batch"], tb["cta_limit"], 0, nne,
+                       c.H, c.I)
+    ok, rel, ratio = cases.within_contract(y.float().cpu().numpy()[rows], oracle.bf16_to_f32(ref_y[rows]))
+    assert ok, f"fc2 rel-L2 {rel:.3e}, worst element at {ratio:.2f}x its bound"
+
+
 @pytest.mark.parametrize("cfg", [dict(T=128, H=1024, I=512, E=16, K=4, shared=0, rs=1.0),
                                  dict(T=333, H=1024, I=512, E=32, K=8, shared=1, rs=2.5),
                                  dict(T=64, H=7168, I=2048, E=8, K=8, shared=1, rs=2.5)])
