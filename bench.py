@@ -222,6 +222,41 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def rank_weights(E, El, e0, dev):
+    """Experts [e0, e0 + El) then the shared expert, from the same synthetic stream as the full set."""
+    import torch
+
+    import k3moe
+
+    w = {}
+    for name, rows_per, K_, seed in (("w13", 2 * I, H, W_SEED13), ("w2", H, I, W_SEED2)):
+        packed = torch.empty(((El + SHARED) * rows_per, K_ // 2), dtype=torch.uint8, device=dev)
+        sf = torch.zeros((El + SHARED) * rows_per // 128 * (K_ // 128) * 512, dtype=torch.uint8, device=dev)
+        per_sf = rows_per // 128 * (K_ // 128) * 512
+        k3moe.synth_mxfp4(seed, El * rows_per, K_, WSD, row0=e0 * rows_per, packed=packed[:El * rows_per],
+                          sf=sf[:El * per_sf])
+        k3moe.synth_mxfp4(seed, rows_per, K_, WSD, row0=E * rows_per, packed=packed[El * rows_per:],
+                          sf=sf[El * per_sf:])
+        w[name], w[name + "_sf"] = packed, sf
+    return w
+
+
+def rank_inputs(T, E, rank, dev):
+    """bf16 x [T, H] ~ N(0, 1) of this rank, router logits S = x.W_router (W_router ~ N(0, 1/H), the same on
+    every rank), bias ~ U(-0.1, 0.1), rs."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn((T, H), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    g.manual_seed(7)
+    wr = torch.randn((H, E), generator=g, device=dev, dtype=torch.float32) / H ** 0.5
+    S = (x.float() @ wr).contiguous()
+    bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
+    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
+    return x, S, bias, rs
+
+
 # ------------------------------------------------------------------ the GPU arm, N > 1: expert parallel
 def run_ep(args, world, rank, dev):
     """Config 4's layout at N GPUs: every rank owns an 8192-row chunk (16 packed sequences) and E/N experts
@@ -234,27 +269,8 @@ def run_ep(args, world, rank, dev):
 
     E, T = args.experts, args.tokens
     El = E // world
-    e0 = rank * El
-    # this rank's weights only: its routed experts then the shared expert (the same synthetic stream as N = 1)
-    w = {}
-    for name, rows_per, K_, seed in (("w13", 2 * I, H, W_SEED13), ("w2", H, I, W_SEED2)):
-        packed = torch.empty(((El + SHARED) * rows_per, K_ // 2), dtype=torch.uint8, device=dev)
-        sf = torch.zeros((El + SHARED) * rows_per // 128 * (K_ // 128) * 512, dtype=torch.uint8, device=dev)
-        per_sf = rows_per // 128 * (K_ // 128) * 512
-        k3moe.synth_mxfp4(seed, El * rows_per, K_, WSD, row0=e0 * rows_per, packed=packed[:El * rows_per],
-                          sf=sf[:El * per_sf])
-        k3moe.synth_mxfp4(seed, rows_per, K_, WSD, row0=E * rows_per, packed=packed[El * rows_per:],
-                          sf=sf[El * per_sf:])
-        w[name], w[name + "_sf"] = packed, sf
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
-    x = torch.randn((T, H), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    g.manual_seed(7)
-    wr = torch.randn((H, E), generator=g, device=dev, dtype=torch.float32) / H ** 0.5
-    S = (x.float() @ wr).contiguous()
-    bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
-    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
-    del wr
+    w = rank_weights(E, El, rank * El, dev)
+    x, S, bias, rs = rank_inputs(T, E, rank, dev)
     layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev)
     for _ in range(args.warmup):
         layer.forward(S, x)
@@ -329,6 +345,112 @@ def run_ep(args, world, rank, dev):
     dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------ decode (config 2): --decode
+DECODE_METRIC = "EP decode us/layer (64 tokens x top-8)"
+
+
+def run_decode(args, world, rank, dev):
+    """Config 2: one MoE decode step of 64 tokens x top-8 over E = 896 experts, expert parallel over the N GPUs
+    (E/N contiguous experts each, 64/N tokens each); the figure is microseconds a layer, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import k3moe
+    import k3moe_ep
+
+    E, Tall = args.experts, args.decode_tokens
+    if Tall % world or E % world:
+        raise SystemExit(f"--decode needs tokens ({Tall}) and experts ({E}) divisible by {world}")
+    T, El = Tall // world, E // world
+    # the same 64 tokens whatever N: rank r owns rows [r T, r T + T) of one global batch
+    x_all, S_all, bias, rs = rank_inputs(Tall, E, 0, dev)
+    x, S = x_all[rank * T:(rank + 1) * T].contiguous(), S_all[rank * T:(rank + 1) * T].contiguous()
+    if world == 1:
+        w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, (E + SHARED) * 2 * I, H, WSD, device=dev)
+        w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, (E + SHARED) * H, I, WSD, device=dev)
+        layer = k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
+        run = lambda xx, SS: layer.forward(SS, xx)  # noqa: E731
+    else:
+        w = rank_weights(E, El, rank * El, dev)
+        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev)
+        run = lambda xx, SS: layer.forward(SS, xx)  # noqa: E731
+    for _ in range(args.warmup):
+        run(x, S)
+    torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # device-resident: steps back to back between two events, max over ranks
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clk:
+        start.record()
+        for _ in range(args.steps):
+            run(x, S)
+        stop.record()
+        torch.cuda.synchronize()
+    us = max_over_ranks(start.elapsed_time(stop) / args.steps * 1e3)
+    # end to end: this rank's x and S from pinned host memory in, its output back, every step
+    x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
+    out_h = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    xd, Sd = torch.empty_like(x), torch.empty_like(S)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = args.e2e_steps or args.steps
+    e0.record()
+    for _ in range(n_e2e):
+        xd.copy_(x_h, non_blocking=True)
+        Sd.copy_(S_h, non_blocking=True)
+        out_h.copy_(run(xd, Sd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_us = max_over_ranks(e0.elapsed_time(e1) / n_e2e * 1e3)
+    # bytes a layer must stream on the slowest rank: its touched experts' weights (+ the shared expert's)
+    if world == 1:
+        off = layer.offsets(T)
+        counts = layer.ws[off["counts"]:off["counts"] + 4 * (E + SHARED)].view(torch.int32).cpu().numpy()
+    else:
+        counts = layer.last["tables"].counts.cpu().numpy()
+    touched = int((counts > 0).sum())
+    per_expert = 2 * I * H // 2 + 2 * I * H // 32 + H * I // 2 + H * I // 32
+    wbytes = max_over_ranks(float(touched * per_expert))
+    hbm_peak, peak_kind = peaks()
+    achieved = wbytes / (us / 1e6) / 1e9
+    if rank == 0:
+        line = {
+            "metric": DECODE_METRIC, "value": us, "unit": "us/layer", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
+            "config": {"workload": "K3-shape decode MoE step (config 2)", "tokens": Tall, "tokens_per_gpu": T,
+                       "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I, "rs": RS,
+                       "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2: each step streams the touched experts' weights"},
+            "roofline": {"kernel": "whole decode layer (weights of the touched experts, slowest rank)",
+                         "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": wbytes,
+                         "traffic": None},
+            "routing": {"touched_experts_max_rank": int(wbytes // per_expert)},
+            "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
+                    "d2h_bytes_per_step": int(x.numel() * 2)},
+            "gpu_launches": (8 if world == 1 else 14) * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------------ the GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -341,6 +463,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=0, help="e2e steps (default: --steps)")
     ap.add_argument("--cpu-tiles", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode", action="store_true", help="config 2: one 64-token decode step, us/layer")
+    ap.add_argument("--decode-tokens", type=int, default=64)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -359,7 +483,9 @@ def main():
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        return run_ep(args, world, rank, dev)
+        return run_decode(args, world, rank, dev) if args.decode else run_ep(args, world, rank, dev)
+    if args.decode:
+        return run_decode(args, world, rank, dev)
     E = args.experts  # noqa: N806  (the routed experts of this run; smaller only for profiling captures)
     T = args.tokens
     k3moe.lib()
