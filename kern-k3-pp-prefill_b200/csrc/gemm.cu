@@ -20,9 +20,10 @@
 // the units round-robin, so the weight blocks of one tile run side by side
 // and its activation tile is read from L2.
 //
-// Roles (320 threads): warp 0 lane 0 issues TMA (operands) and bulk copies
-// (scale atoms); warp 1 lane 0 copies the scale atoms into tensor memory
-// (tcgen05.cp) and issues the MMAs; warps 2-9 are the epilogue.  An epilogue
+// Roles (384 threads): warp 0 lane 0 issues the TMA boxes (activation tile,
+// two weight tiles); warps 10-11 bring the three scale atoms of a stage with
+// cp.async; warp 1 lane 0 copies the atoms into tensor memory (tcgen05.cp)
+// and issues the MMAs; warps 2-9 are the epilogue.  An epilogue
 // warp reads its sub-partition's 32 token rows and one half of the columns
 // into registers, releases the accumulator, and only then computes and
 // stores, so the next unit's MMAs overlap the math and the stores.  A 4-stage
@@ -49,12 +50,21 @@ constexpr int OPS_STAGE = A_BYTES + B_BYTES;                  // 48 KB, 1024-ali
 constexpr int SF_STAGE = 3 * SF_BYTES;                        // activation atom + two weight atoms
 // bytes a stage's copies complete on its barrier: a 16U4_ALIGN16B load counts
 // the packed (global) bytes, half the unpacked tile it writes
-constexpr u32 STAGE_TX = A_BYTES + B_BYTES / 2 + SF_STAGE;
+#ifndef K3MOE_LDGSTS
+#define K3MOE_LDGSTS 1
+#endif
+// 1: a stage's three 512-byte scale atoms travel by cp.async (LDGSTS) from two loader warps, leaving the
+// TMA unit three large boxes a stage (measured 1.5% faster a layer than six TMA operations); 0: all by TMA.
+// Moving the 16 KB activation tile to cp.async as well starved the MMA (FC1 3.06 -> 3.94 ms).
+constexpr int LDGSTS = K3MOE_LDGSTS;
+constexpr u32 STAGE_TX = LDGSTS ? A_BYTES + B_BYTES / 2 : A_BYTES + B_BYTES / 2 + SF_STAGE;
 constexpr int SMEM_BYTES = STAGES * (OPS_STAGE + SF_STAGE) + 1024 /*align*/ + 256 /*barriers*/;
 constexpr u32 TMEM_COLS = 512;
 constexpr int SF_TMEM_COL = BN;          // scale columns after the accumulator
 constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr int LOADER_WARPS = LDGSTS ? 2 : 0;
+constexpr int LOADER_THREADS = 32 * LOADER_WARPS;
+constexpr int THREADS = 32 * (2 + EPI_WARPS + LOADER_WARPS);
 }  // namespace gemm
 
 enum { MODE_FC1 = 0, MODE_FC2 = 1 };
@@ -137,7 +147,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + LOADER_THREADS);  // the TMA producer's arrive + one per loader thread
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -210,12 +220,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           // maps (one contiguous chunk), and its scales are the 512-byte atom t
           const int ta = (w.row0 / BM) * kstages + ks;
           tma_load_2d(st, &tmA, &full[stage], 0, ta * BM);
-          bulk_load(sf, p.sfa + (long long)ta * SF_BYTES, SF_BYTES, &full[stage]);
+          if (!LDGSTS) bulk_load(sf, p.sfa + (long long)ta * SF_BYTES, SF_BYTES, &full[stage]);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int t = (wrow[h] / 128) * kstages + ks;
             tma_load_2d(st + A_BYTES + h * W_TILE, &tmW, &full[stage], 0, t * 128);
-            bulk_load(sf + (1 + h) * SF_BYTES, p.sfw + (long long)t * SF_BYTES, SF_BYTES, &full[stage]);
+            if (!LDGSTS) bulk_load(sf + (1 + h) * SF_BYTES, p.sfw + (long long)t * SF_BYTES, SF_BYTES, &full[stage]);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -255,6 +265,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             break;
           }
           t_wfull += clock64() - t0;
+          // the loader warps' cp.async writes (generic proxy) before the tensor core's reads (async proxy)
+          if (LDGSTS) fence_proxy_async_shared();
           tc_fence_after();
           const u32 st = smem_u32(ops + stage * OPS_STAGE);
           const u32 sf = smem_u32(sfs + stage * SF_STAGE);
@@ -293,6 +305,38 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         atomicAdd(p.trace + MODE * 16 + 7, (unsigned long long)n_units);
       }
     }
+  } else if (warp >= 2 + EPI_WARPS) {
+    // ------------------------------------------------ cp.async loaders (warps 10, 11): a stage's scale atoms
+    // (the activation atom, then the two weight atoms), 16 bytes a thread-copy
+    const int lt = threadIdx.x - 32 * (2 + EPI_WARPS);
+    int stage = 0;
+    u32 phase = 0;
+    bool stop = false;
+    for (int u = blockIdx.x; u < units && !stop && !*abort_flag; u += gridDim.x) {
+      const Unit w = decode_unit(p, u);
+      if (!w.valid) continue;
+      const int wt0 = weight_row<MODE>(p, w, 0) / 128, wt1 = weight_row<MODE>(p, w, 1) / 128;
+      for (int ks = 0; ks < kstages; ++ks) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, 0x800u + MODE)) {
+          stop = true;
+          break;
+        }
+        const u32 sf = smem_u32(sfs + stage * SF_STAGE);
+        const int ta = (w.row0 / BM) * kstages + ks;
+        for (int c = lt; c < SF_STAGE / 16; c += LOADER_THREADS) {
+          const int q = c >> 5;  // atom: 0 activation, 1 and 2 the weight tiles
+          const long long t = q == 0 ? ta : (long long)(q == 1 ? wt0 : wt1) * kstages + ks;
+          const uint8_t* a = (q == 0 ? p.sfa : p.sfw) + t * SF_BYTES;
+          cp_async16(sf + c * 16, a + (c & 31) * 16);
+        }
+        cp_async_mbar_arrive_noinc(&full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    cp_async_wait_all();
   } else {
     // ------------------------------------------------ epilogue (warps 2..9)
     // warp -> (sub-partition, column half): its thread i owns token row 32*sub + i of the tile
