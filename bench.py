@@ -369,13 +369,19 @@ def run_decode(args, world, rank, dev):
         w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, (E + SHARED) * 2 * I, H, WSD, device=dev)
         w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, (E + SHARED) * H, I, WSD, device=dev)
         layer = k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
-        run = lambda xx, SS: layer.forward(SS, xx)  # noqa: E731
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        run = lambda: layer.forward(S, x, out)  # noqa: E731
     else:
+        # fixed-size all-to-all blocks: no host synchronisation in the step, so it can be graph-captured
         w = rank_weights(E, El, rank * El, dev)
-        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev)
-        run = lambda xx, SS: layer.forward(SS, xx)  # noqa: E731
-    for _ in range(args.warmup):
-        run(x, S)
+        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T)
+        run = lambda: layer.forward(S, x)  # noqa: E731
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(args.warmup):
+            run()
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
 
     def max_over_ranks(v):
@@ -385,32 +391,55 @@ def run_decode(args, world, rank, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # device-resident: steps back to back between two events, max over ranks
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    with ClockSampler(uuid) as clk:
+    def timed(step):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         start.record()
         for _ in range(args.steps):
-            run(x, S)
+            step()
         stop.record()
         torch.cuda.synchronize()
-    us = max_over_ranks(start.elapsed_time(stop) / args.steps * 1e3)
-    # end to end: this rank's x and S from pinned host memory in, its output back, every step
+        return max_over_ranks(start.elapsed_time(stop) / args.steps * 1e3)
+
+    eager_us = timed(run)
+    # the whole step (its NCCL calls included) as one CUDA graph, replayed
+    graph, graph_note = None, None
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = run()
+        graph.replay()
+        torch.cuda.synchronize()
+    except Exception as ex:  # capture unsupported here: the eager step is the figure
+        graph, graph_note = None, f"graph capture failed: {type(ex).__name__}: {str(ex)[:120]}"
+    ok = torch.tensor([1.0 if graph is not None else 0.0], device=dev)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if ok.item() < 1.0:
+        graph = None
+    step = graph.replay if graph is not None else run
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(uuid) as clk:
+        us = timed(step)
+    # end to end: this rank's x and S from pinned host memory into the step's inputs, its output back
     x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
     out_h = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-    xd, Sd = torch.empty_like(x), torch.empty_like(S)
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_e2e = args.e2e_steps or args.steps
     e0.record()
     for _ in range(n_e2e):
-        xd.copy_(x_h, non_blocking=True)
-        Sd.copy_(S_h, non_blocking=True)
-        out_h.copy_(run(xd, Sd), non_blocking=True)
+        x.copy_(x_h, non_blocking=True)
+        S.copy_(S_h, non_blocking=True)
+        if graph is not None:
+            graph.replay()
+            o = static_out
+        else:
+            o = run()
+        out_h.copy_(o, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e_us = max_over_ranks(e0.elapsed_time(e1) / n_e2e * 1e3)
@@ -442,10 +471,19 @@ def run_decode(args, world, rank, dev):
             "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
                     "d2h_bytes_per_step": int(x.numel() * 2)},
             "gpu_launches": (8 if world == 1 else 14) * args.steps,
+            "cuda_graph": graph is not None, "eager_us": eager_us,
             "clocks": clk.summary(),
             "cpu_baseline": None,
         }
+        if graph_note:
+            line["note"] = graph_note
         print(json.dumps(line), flush=True)
+    # a graph holding NCCL calls is released before the process group goes (step holds a reference too)
+    step = None
+    if graph is not None:
+        graph.reset()
+    del graph
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -543,16 +581,21 @@ def main():
     k3moe.set_trace(None)
     tr = trace.cpu().tolist()
     gemm_trace = {}
+    stage_ms = np.array([[ev[s][i].elapsed_time(ev[s][i + 1]) for i in range(6)] for s in range(args.steps)]).mean(0)
     for mode, name in ((0, "fc1"), (1, "fc2")):
         c = dict(zip(k3moe.TRACE_FIELDS, tr[16 * mode:16 * mode + 8]))
+        # the MMA role's clock64 cycles a block over the kernel's event time: the SM clock the GEMM ran at
+        # (NVML's samples miss the power-capped dips inside the GEMMs)
+        blocks = min(torch.cuda.get_device_properties(dev).multi_processor_count, max(int(c["units"]), 1))
+        sm_mhz = c["mma"] / 2 / blocks / (float(stage_ms[3 + mode]) * 1e3)
         gemm_trace[name] = {
+            "sm_mhz_in_kernel": round(sm_mhz),
             "mma_busy": round(1 - (c["mma_wait_loaded"] + c["mma_wait_drained"]) / max(c["mma"], 1), 3),
             "mma_wait_loaded": round(c["mma_wait_loaded"] / max(c["mma"], 1), 3),
             "mma_wait_drained": round(c["mma_wait_drained"] / max(c["mma"], 1), 3),
             "producer_wait_stage": round(c["producer_wait_stage"] / max(c["producer"], 1), 3),
             "epilogue_busy": round(1 - c["epilogue_wait_acc"] / max(c["epilogue"], 1), 3),
         }
-    stage_ms = np.array([[ev[s][i].elapsed_time(ev[s][i + 1]) for i in range(6)] for s in range(args.steps)]).mean(0)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

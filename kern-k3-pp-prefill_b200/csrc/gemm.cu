@@ -38,10 +38,6 @@ constexpr int BM = 128;                  // token rows a tile (the routing tile)
 constexpr int BN = 256;                  // weight rows a unit: the MMA's N
 constexpr int BK = 128;                  // K elements a stage
 constexpr int STAGES = 4;
-#ifndef K3MOE_PREFETCH
-#define K3MOE_PREFETCH 0
-#endif
-constexpr int PREFETCH = K3MOE_PREFETCH;  // k-stages an L2 prefetch runs ahead of the loads (0: none)
 constexpr int A_BYTES = BM * BK;         // activation tile (E4M3)
 constexpr int W_TILE = 128 * BK;         // one 128-row weight tile, unpacked E2M1 (a byte an element)
 constexpr int B_BYTES = 2 * W_TILE;
@@ -175,29 +171,6 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
       int armed[STAGES] = {0, 0, 0, 0};
       const long long t_role = clock64();
       long long t_wait = 0;
-      // optional L2 prefetch cursor PREFETCH stages ahead of the shared-memory loads
-      int pu = blockIdx.x, pks = 0;
-      Unit pw = {};
-      if (PREFETCH > 0 && pu < units) pw = decode_unit(p, pu);
-      auto prefetch_next = [&]() {
-        while (pu < units && !pw.valid) {
-          pu += gridDim.x;
-          if (pu < units) pw = decode_unit(p, pu);
-        }
-        if (pu >= units) return;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int t = (weight_row<MODE>(p, pw, h) / 128) * kstages + pks;
-          tma_prefetch_2d(&tmW, 0, t * 128);
-          bulk_prefetch(p.sfw + (long long)t * SF_BYTES, SF_BYTES);
-        }
-        if (++pks == kstages) {
-          pks = 0;
-          pu += gridDim.x;
-          if (pu < units) pw = decode_unit(p, pu);
-        }
-      };
-      for (int i = 0; i < PREFETCH; ++i) prefetch_next();
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         const Unit w = decode_unit(p, u);
         if (!w.valid) {
@@ -208,7 +181,6 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         wrow[0] = weight_row<MODE>(p, w, 0);
         wrow[1] = weight_row<MODE>(p, w, 1);
         for (int ks = 0; ks < kstages; ++ks) {
-          if (PREFETCH > 0) prefetch_next();
           const long long t0 = clock64();
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, 0x200u + MODE)) break;
           t_wait += clock64() - t0;

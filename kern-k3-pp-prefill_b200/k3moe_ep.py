@@ -51,10 +51,10 @@ class GpuOps:
     def stride(self, H):
         return k3moe.lib().k3moe_ep_row_stride(H)
 
-    def pack(self, x, idx, send_pos, E_local, n_slots):
+    def pack(self, x, idx, send_pos, E_local, n_slots, out=None):
         H = x.shape[1]
         st = self.stride(H)
-        buf = torch.empty((n_slots, st), dtype=torch.uint8, device=x.device)
+        buf = torch.empty((n_slots, st), dtype=torch.uint8, device=x.device) if out is None else out
         k3moe._check(k3moe.lib().k3moe_ep_pack(x.data_ptr(), x.stride(0), x.shape[0], H, idx.shape[1], idx.data_ptr(),
                                                send_pos.data_ptr(), E_local, 0, buf.data_ptr(), st,
                                                k3moe._stream()), "ep_pack")
@@ -107,7 +107,11 @@ class EPMoELayer:
     [rank*E_local, (rank+1)*E_local)) and, with `shared`, the shared expert as local expert E_local.
     """
 
-    def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None):
+    def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None, fixed_tokens=None):
+        """fixed_tokens: when set (at most that many tokens a call), every rank sends fixed-size blocks of
+        fixed_tokens*K slots to every rank, empty slots marked by local expert id -1: no host
+        synchronisation, so a whole step can be captured in a CUDA graph (decode-sized batches)."""
+        self.fixed_tokens = fixed_tokens
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -127,8 +131,47 @@ class EPMoELayer:
         dist.all_to_all_single(ob, ib, [r * row_bytes for r in out_rows], [r * row_bytes for r in in_rows],
                                group=self.group)
 
+    def _forward_fixed(self, S, x):
+        """forward() with fixed-size all-to-all blocks: cap = fixed_tokens * K slots a destination."""
+        ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
+        T = x.shape[0]
+        if T > self.fixed_tokens:
+            raise ValueError(f"{T} tokens exceed fixed_tokens={self.fixed_tokens}")
+        cap = self.fixed_tokens * K
+        idx, wts = ops.topk(S, self.bias, self.rs, K)
+        dest = torch.div(idx, El, rounding_mode="floor").to(torch.int32)
+        plan = ops.tables(dest.reshape(-1, 1).contiguous(), W, 1)
+        counts = plan.counts[:W]
+        first = (torch.cumsum(counts, 0, dtype=torch.int32) - counts).to(torch.int64)
+        d = dest.reshape(-1).to(torch.int64)
+        # slot of pick (t, k): its destination's block, then its rank among that destination's picks
+        slot = (d * cap + plan.exp2perm.reshape(-1).to(torch.int64) - first[d]).to(torch.int32).reshape(T, K)
+        stride = ops.stride(H)
+        n_slots = W * cap
+        send = torch.empty((n_slots, stride), dtype=torch.uint8, device=x.device)
+        eid_col = H + H // 32
+        send[:, eid_col:eid_col + 4].view(torch.int32).fill_(-1)  # empty slots: no expert
+        ops.pack(x, idx, slot, El, n_slots, out=send)
+        R = n_slots + (T if self.shared else 0)
+        recv = torch.empty((R, stride), dtype=torch.uint8, device=x.device)
+        dist.all_to_all_single(recv[:n_slots].reshape(-1), send.reshape(-1), group=self.group)
+        if self.shared:
+            ops.pack_rows(x, El, recv[n_slots:R])
+        ids = ops.ids(recv, R, H)
+        tb = ops.tables(ids, El + self.shared, 128)
+        qp, sfp = ops.unpack(recv, R, H, tb)
+        y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, R)
+        back = torch.empty((n_slots, H), dtype=y.dtype, device=y.device)
+        dist.all_to_all_single(back.reshape(-1).view(torch.uint8), y[:n_slots].reshape(-1).view(torch.uint8),
+                               group=self.group)
+        self.last = {"received_rows": None, "sent_rows": T * K, "tables": tb}
+        shared_rows = y[n_slots:R] if self.shared else None
+        return ops.combine(back, slot, wts, shared_rows, T, K, H)
+
     def forward(self, S, x, events=None):
         """events: optional {"dispatch", "fc1", "combine": (start, end)} CUDA events to record."""
+        if self.fixed_tokens is not None:
+            return self._forward_fixed(S, x)
         ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
         T = x.shape[0]
         idx, wts = ops.topk(S, self.bias, self.rs, K)

@@ -44,10 +44,10 @@ class OracleOps:
         q, sf = oracle.quant_mxfp8(_bits(x), tiled=False)
         return q, sf
 
-    def pack(self, x, idx, send_pos, E_local, n_slots):
+    def pack(self, x, idx, send_pos, E_local, n_slots, out=None):
         H = x.shape[1]
         q, sf = self._rows(x)
-        buf = np.zeros((n_slots, self.stride(H)), np.uint8)
+        buf = np.zeros((n_slots, self.stride(H)), np.uint8) if out is None else _np(out)
         idx, pos = _np(idx), _np(send_pos)
         for t in range(idx.shape[0]):
             for k in range(idx.shape[1]):
@@ -55,7 +55,7 @@ class OracleOps:
                 buf[p, :H] = q[t]
                 buf[p, H:H + H // 32] = sf[t]
                 buf[p, H + H // 32:H + H // 32 + 4] = np.array([idx[t, k] % E_local], np.int32).view(np.uint8)
-        return torch.from_numpy(buf)
+        return torch.from_numpy(buf) if out is None else out
 
     def pack_rows(self, x, eid, dst):
         H = x.shape[1]
@@ -102,6 +102,6 @@ class OracleOps:
         meta = None
         if shared_rows is not None:
             fc2 = np.concatenate([fc2, _bits(shared_rows)])
-            meta = np.array([0, 0, T * K, 0], np.int32)
+            meta = np.array([0, 0, back.shape[0], 0], np.int32)  # the shared rows follow every returned row
         out = oracle.combine(fc2, _np(send_pos), _np(wts), meta, T, K)
         return _bf16(out)

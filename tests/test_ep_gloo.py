@@ -24,7 +24,7 @@ def _free_port():
 CFG = dict(T=96, H=256, I=256, E=8, K=2, shared=1, rs=2.5, seed=11)
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, fixed):
     import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
@@ -45,18 +45,21 @@ def _worker(rank, world, port, outdir):
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
     w = k3moe_ep.slice_weights(t(c.w13), t(c.w13_sf), t(c.w2), t(c.w2_sf), c.E, c.shared, rank, world, c.H, c.I)
     rs = t(np.array([c.rs_bits], np.uint16)).view(torch.bfloat16)
-    layer = k3moe_ep.EPMoELayer(c.H, c.I, c.E, c.K, c.shared, w, t(c.bias), rs, ops=ep_oracle_ops.OracleOps())
+    layer = k3moe_ep.EPMoELayer(c.H, c.I, c.E, c.K, c.shared, w, t(c.bias), rs, ops=ep_oracle_ops.OracleOps(),
+                                fixed_tokens=T_l if fixed else None)
     out = layer.forward(t(c.S[rows]), t(c.x_bits[rows]).view(torch.bfloat16))
     np.save(os.path.join(outdir, f"out{rank}.npy"), out.view(torch.int16).numpy().view(np.uint16))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_ep2_gloo_matches_single_device():
+@pytest.mark.parametrize("fixed", [False, True])
+def test_ep2_gloo_matches_single_device(fixed):
+    # fixed: the fixed-block all-to-all (no counts exchange, empty slots marked -1) of decode-sized batches
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, d)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, fixed)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:

@@ -1,6 +1,8 @@
 """Expert parallelism on 2 GPUs over NCCL: every rank holds half the experts
 and its own tokens; the layer's output must equal, bit for bit, the single-GPU
-layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs."""
+layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs.  Three
+modes: the counts-exchange all-to-all, the fixed-block all-to-all, and the
+fixed-block step captured in a CUDA graph (NCCL calls inside) and replayed."""
 import multiprocessing as mp
 import os
 import socket
@@ -22,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, mode):
     import datetime
     import sys
 
@@ -56,8 +58,26 @@ def _worker(rank, world, port, outdir):
     rs = torch.tensor([c["rs"]], dtype=torch.bfloat16, device=dev)
     rows = slice(rank * c["T_local"], (rank + 1) * c["T_local"])
     w = k3moe_ep.slice_weights(w13, w13_sf, w2, w2_sf, E, sh, rank, world, H, I)
-    layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev)
-    outs = [layer.forward(S[rows].contiguous(), x[rows].contiguous()) for _ in range(2)]  # twice: reused buffers
+    layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev,
+                                fixed_tokens=c["T_local"] if mode != "counts" else None)
+    xs, Ss = x[rows].contiguous(), S[rows].contiguous()
+    graph = None
+    if mode == "graph":
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                layer.forward(Ss, xs)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = layer.forward(Ss, xs)
+        outs = []
+        for _ in range(2):
+            graph.replay()
+            outs.append(static_out.clone())
+    else:
+        outs = [layer.forward(Ss, xs) for _ in range(2)]  # twice: reused buffers
     full = [torch.empty_like(outs[1]) for _ in range(world)]
     dist.all_gather(full, outs[1])
     torch.cuda.synchronize()
@@ -73,17 +93,22 @@ def _worker(rank, world, port, outdir):
         ok = ok and not bad_rows
         open(os.path.join(outdir, "result"), "w").write(
             "ok" if ok else f"mismatch: repeat-equal={ok} rows={bad_rows[:20]} n={len(bad_rows)} maxdiff={diff}")
+    if graph is not None:  # a graph holding NCCL calls is released before the process group goes
+        graph.reset()
+    del graph
+    torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_ep2_nccl_bit_identical_to_one_gpu():
+@pytest.mark.parametrize("mode", ["counts", "fixed", "graph"])
+def test_ep2_nccl_bit_identical_to_one_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs (run with gpurun --gpus 2)")
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, d)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, mode)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
