@@ -503,6 +503,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode", action="store_true", help="config 2: one 64-token decode step, us/layer")
     ap.add_argument("--decode-tokens", type=int, default=64)
+    ap.add_argument("--zipf", action="store_true",
+                    help="config 3: the routing bias makes expert popularity Zipf(1.1) (N = 1 prefill)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -541,6 +543,13 @@ def main():
     bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
     rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
     del wr
+    zipf = None
+    if args.zipf:  # config 3: bias fitted (on the host) so the realised top-8 histogram follows Zipf(1.1)
+        import cases
+
+        zb, beta, kl = cases.zipf_bias(S.cpu().numpy(), K)
+        bias = torch.from_numpy(zb).to(dev)
+        zipf = {"s": 1.1, "seed": 3, "beta": beta, "kl": round(kl, 4)}
     layer = k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
     out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
 
@@ -619,7 +628,7 @@ def main():
     # profiles/grouped_gemm_fc1_config1_traffic.md (line "bytes_per_launch: N")
     traffic = None
     tf = os.path.join(ROOT, "profiles", "grouped_gemm_fc1_config1_traffic.md")
-    if os.path.exists(tf) and T == T_DEF and E == 896:
+    if os.path.exists(tf) and T == T_DEF and E == 896 and not args.zipf:
         for ln in open(tf):
             if ln.startswith("bytes_per_launch:"):
                 traffic = int(ln.split(":")[1].strip())
@@ -696,7 +705,9 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
-            "config": {"workload": "K3-shape prefill MoE layer (config 1)", "T": T, "H": H, "I": I, "E": E, "K": K,
+            "config": {"workload": ("K3-shape prefill MoE layer, Zipf(1.1) expert popularity (config 3)" if zipf else
+                                    "K3-shape prefill MoE layer (config 1)"), "zipf": zipf,
+                       "T": T, "H": H, "I": I, "E": E, "K": K,
                        "shared_expert_width": I, "rs": RS, "global_batch": T * world, "seq_len": T,
                        "sequences": 16, "cu_seqlens": cu_seqlens(T).tolist(),
                        "parallelism": f"dp{world} (experts replicated per GPU)" if world > 1 else "ep1",
@@ -704,7 +715,8 @@ def main():
             "tflops": flops / (ms / 1e3) / 1e12,
             "pct_fp8_peak": flops / (ms / 1e3) / 1e12 / (FP8_PEAK_TFLOPS * world) * 100,
             "stage_ms": dict(zip(k3moe.MoELayer.STAGES, [round(float(v), 4) for v in stage_ms])),
-            "routing": {"num_non_exiting": nne, "routed_rows": routed_rows, "touched_experts": touched},
+            "routing": {"num_non_exiting": nne, "routed_rows": routed_rows, "touched_experts": touched,
+                        "empty_experts": int((counts[:E] == 0).sum()), "max_expert_rows": int(counts[:E].max())},
             "roofline": {"kernel": "FC1 grouped GEMM (grouped_gemm_kernel<0>)", "bound": "hbm",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                          "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes,

@@ -100,3 +100,27 @@ def within_contract(got, ref, rel_tol=1e-2, abs_tol=2e-2):
     bound = np.maximum(abs_tol, 3 * bf16_ulp(ref) + 1e-3)
     ratio = float((np.abs(got - ref) / bound).max()) if got.size else 0.0
     return rel <= rel_tol and ratio <= 1.0, rel, ratio
+
+
+def zipf_bias(S, K, s=1.1, seed=3, betas=None):
+    """Config 3's routing bias: expert popularity ~ Zipf(s) over a seeded permutation of the experts.
+
+    bias_e = -s * beta * ln(rank_e) (rank 1 = most popular), with beta the value on a log grid whose realised
+    top-K histogram over the logits S [T, E] has the smallest KL divergence to the Zipf law.  Returns
+    (bias f32 [E], beta, kl)."""
+    S = np.asarray(S, np.float32)
+    T, E = S.shape
+    rank = np.empty(E, np.int64)
+    rank[np.random.default_rng(seed).permutation(E)] = np.arange(1, E + 1)
+    zipf = rank.astype(np.float64) ** -s
+    zipf /= zipf.sum()
+    sig = 1.0 / (1.0 + np.exp(-S.astype(np.float64)))
+    best = None
+    for beta in (np.geomspace(1e-3, 1.0, 61) if betas is None else betas):
+        bias = (-s * beta * np.log(rank)).astype(np.float32)
+        top = np.argpartition(-(sig + bias), K, axis=1)[:, :K]
+        h = np.bincount(top.ravel(), minlength=E) / (T * K)
+        kl = float(np.sum(np.where(h > 0, h * np.log(np.maximum(h, 1e-30) / zipf), 0.0)))
+        if best is None or kl < best[2]:
+            best = (bias, float(beta), kl)
+    return best

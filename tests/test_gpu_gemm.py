@@ -156,3 +156,27 @@ def test_layer_repeatable(dev):
     b = layer.forward(g["S"], g["x"]).clone()
     torch.cuda.synchronize()
     assert torch.equal(a.view(torch.int16), b.view(torch.int16)), "the layer is not deterministic"
+
+
+def test_layer_zipf_skew(dev):
+    # config 3's routing at a small size: Zipf(1.1) popularity leaves many experts empty and a few with
+    # several tiles of rows (ragged tiles, empty groups)
+    cfg = dict(T=1024, H=512, I=256, E=256, K=8, shared=1, rs=2.5, seed=13)
+    c0 = cases.make_case(**cfg)
+    bias, _, _ = cases.zipf_bias(c0.S, cfg["K"])
+    c = cases.make_case(**cfg, bias=bias)
+    ref_out, inter = cases.oracle_forward(c)
+    counts = np.bincount(inter["idx"].ravel(), minlength=c.E)
+    assert (counts == 0).sum() >= 8 and counts.max() > 256, counts
+    g = cases.to_device(c, dev)
+    layer = k3moe.MoELayer(c.H, c.I, c.E, c.K, c.shared, g["w13"], g["w13_sf"], g["w2"], g["w2_sf"], g["bias"],
+                           g["rs"], max_tokens=c.T, device=dev)
+    out = layer.forward(g["S"], g["x"])
+    torch.cuda.synchronize()
+    layer.check_device_error(c.T)
+    ok, rel, ratio = cases.within_contract(out.float().cpu().numpy(), oracle.bf16_to_f32(ref_out))
+    assert ok, f"zipf layer rel-L2 {rel:.3e}, worst element at {ratio:.2f}x its bound"
+    off = layer.offsets(c.T)
+    ws = layer.ws.cpu().numpy()
+    e2p = ws[off["exp2perm"]:off["exp2perm"] + c.T * c.K * 4].view(np.int32).reshape(c.T, c.K)
+    assert np.array_equal(e2p, inter["tables"]["exp2perm"])

@@ -127,3 +127,15 @@ def test_oracle_layer_is_close_to_fp64_math():
     assert np.isfinite(a).all() and np.isfinite(f1).all()
     y = oracle.bf16_to_f32(out)
     assert np.isfinite(y).all() and np.abs(y).max() > 0
+
+
+def test_zipf_bias_shapes_routing():
+    # config 3's construction: many empty experts, a heavy head, and a better fit than no bias
+    rng = np.random.default_rng(0)
+    S = rng.standard_normal((1024, 128)).astype(np.float32)
+    bias, beta, kl = cases.zipf_bias(S, 8)
+    idx, _ = oracle.topk(S, bias, 0x3F80, 8)
+    h = np.bincount(idx.ravel(), minlength=128)
+    _, _, kl0 = cases.zipf_bias(S, 8, betas=[0.0])
+    assert beta > 0 and kl < kl0
+    assert (h == 0).sum() >= 3 and h.max() > 8 * h.mean()
