@@ -14,6 +14,8 @@
 //   kern_k3_moe_finalize        source/k3_moe_prefill.cu:206  grid rows, any block
 //   kern_k3g_finalize_rms       source/k3_prefill_glue.cu:573 grid rows, block cols/8
 //   kern_k3g_moe_finalize_rms   source/k3_moe_route.cu:538    grid rows, block 448
+//   kern_k3g_moe_route          source/k3_moe_route.cu:338    grid 64 (B <= 256) or 288, block 512 (grid barrier)
+//   kern_k3g_moe_route_init     source/k3_moe_route.cu:522    any grid, block 1024
 #include "common.cuh"
 
 namespace k3 {
@@ -266,4 +268,255 @@ extern "C" __global__ void __launch_bounds__(dropin::LATENT / 8) kern_k3g_moe_fi
     const bf16* __restrict__ fc2, const int* __restrict__ exp2perm, const float* __restrict__ wts,
     const bf16* __restrict__ gamma, bf16* __restrict__ out, int ldo, int T) {
   finalize_rms_row(fc2, exp2perm, wts, gamma, out + (long long)blockIdx.x * ldo, T, dropin::LATENT);
+}
+
+// ------------------------------------------------------------------ the fused prefill front (one launch)
+// kern_k3g_moe_route (source/k3_moe_route.cu:338-520, op scripts/k3_moe_bmm.py:96-100): router top-16,
+// the latent in MXFP8 (linear scales), the shared expert's SiTU activation and the routing tables of a rank
+// holding every expert, `tile` rows a CTA, in one launch.  Grid 64 (B <= 256) or 288 blocks of 512 threads,
+// two an SM, every block resident: phase 1 (rows' top-k and their marks in this call's table; the latent
+// and shared-activation pieces) | grid barrier | phase 2 (counts scanned into CTA offsets, the CTA tables,
+// every pick's permuted row in row order).
+//
+// `sync` (SYNC_WORDS u32, zeroed once by kern_k3g_moe_route_init): word 0 the barrier's arrivals, word 32
+// its generation, word 1 an error word (nonzero: a barrier wait ran out, the outputs are incomplete), then
+// two routing tables picked by the generation's parity: [E] pick counts, [E][32] counts per 256-row chunk,
+// [E][256] row bitmaps.  A call zeroes the other parity's table for the next call, so calls of any B need no
+// re-initialisation.  The sizes are the reference's (the manifest allocates the buffer).
+namespace k3 {
+namespace dropin {
+constexpr int SHARED_W = 6144;               // the shared expert's width: gu = [gate | up], act = SiTU(gate, up)
+constexpr int MAX_ROWS = 8192;
+constexpr int CHUNK = 256, CHUNKS = MAX_ROWS / CHUNK, WORDS = MAX_ROWS / 32;
+constexpr int TABLE = EXPERTS * (1 + CHUNKS + WORDS);
+constexpr int ARRIVE_AT = 0, ERR_AT = 1, GEN_AT = 32, TABLES_AT = 64;
+constexpr int SYNC_WORDS = TABLES_AT + 2 * TABLE + 2;
+constexpr int RT_THREADS = 512, RT_WARPS = RT_THREADS / 32;
+constexpr u64 BARRIER_LIMIT_NS = 2000000000ull;
+}  // namespace dropin
+
+__device__ __forceinline__ u32 ld_acquire_gpu(const u32* p) {
+  u32 v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(u32* p, u32 v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ float tanh_approx(float x) {
+  float r;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float ex2_approx_ftz(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// The shared expert's activation as the reference's fused front computes it (source/k3_moe_route.cu:257-269,
+// k3_prefill_glue.cu's kern_k3g_situ): e^-g as ex2.approx.ftz(g * -log2 e), the sigmoid an IEEE reciprocal,
+// the tanh terms tanh.approx, every product and sum rounded on its own: (4 tanh(g/4) * sigmoid(g)) * 25 tanh(u/25).
+__device__ __forceinline__ float situ_front(float g, float u) {
+  const float d = __fadd_rn(ex2_approx_ftz(__fmul_rn(g, -1.44269502f)), 1.0f);
+  const float a = __fmul_rn(tanh_approx(__fmul_rn(g, 0.25f)), 4.0f);
+  const float c = __fmul_rn(tanh_approx(__fmul_rn(u, 0.04f)), 25.0f);
+  return __fmul_rn(__fmul_rn(a, __frcp_rn(d)), c);
+}
+
+// One warp a row: keys ord(sigmoid(S) + bias) of experts j*32 + lane, the K largest (ties to the smaller
+// expert), lane r < K ending with the r-th pick; its weight is the pick's sigmoid over the picks' butterfly
+// sum, times rs: kern_k3g_router_topk's values (topk_warp) with the keys alone held in registers.
+template <int EPL>
+__device__ __forceinline__ int topk_keys_warp(const float* __restrict__ row, const float* __restrict__ bias, int K,
+                                              float rsv, int lane, int* __restrict__ idx_out,
+                                              float* __restrict__ wts_out) {
+  u32 o[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int e = j * 32 + lane;
+    o[j] = ord_f32(1.0f / (1.0f + expf(-row[e])) + bias[e]);
+  }
+  int pick = 0;
+  for (int r = 0; r < K; ++r) {
+    u32 m = o[0];
+#pragma unroll
+    for (int j = 1; j < EPL; ++j) m = max(m, o[j]);
+    m = __reduce_max_sync(0xffffffffu, m);
+    u32 mine = 0xffffffffu;
+#pragma unroll
+    for (int j = EPL - 1; j >= 0; --j)
+      if (o[j] == m) mine = (u32)(j * 32 + lane);
+    const u32 ew = __reduce_min_sync(0xffffffffu, mine);
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (j * 32 + lane == (int)ew) o[j] = 0u;
+    if (lane == r) pick = (int)ew;
+  }
+  const float w = lane < K ? 1.0f / (1.0f + expf(-row[pick])) : 0.f;
+  float den = w;
+  for (int off = K / 2; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+  if (lane < K) {
+    wts_out[lane] = (w / (den + 1e-20f)) * rsv;
+    idx_out[lane] = pick;
+  }
+  return pick;
+}
+
+}  // namespace k3
+
+extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe_route(
+    const float* __restrict__ S, const float* __restrict__ bias, const bf16* __restrict__ rs,
+    const bf16* __restrict__ x, int ldx, const bf16* __restrict__ gu, int ldgu, uint8_t* __restrict__ q,
+    uint8_t* __restrict__ sf, int* __restrict__ idx, float* __restrict__ wts, bf16* __restrict__ act, int ldact,
+    u32* __restrict__ sync, int* __restrict__ cta_batch, int* __restrict__ cta_limit,
+    int* __restrict__ num_non_exiting, int* __restrict__ total_padded, int* __restrict__ route_map,
+    int* __restrict__ exp2perm, int tile, int B) {
+  using namespace k3::dropin;
+  __shared__ u32 s_gen, s_ok;
+  __shared__ int s_cnt[EXPERTS], s_off[EXPERTS];
+  __shared__ int s_wsum[RT_WARPS];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int nthreads = gridDim.x * RT_THREADS, gt = blockIdx.x * RT_THREADS + t;
+  const int gwarp = blockIdx.x * RT_WARPS + warp, nwarps = gridDim.x * RT_WARPS;
+  if (B < 0 || B > MAX_ROWS || tile < 1) return;  // every block returns alike: no barrier is entered
+
+  if (t == 0) s_gen = ld_acquire_gpu(sync + GEN_AT);
+  __syncthreads();
+  const u32 gen = s_gen;
+  u32* cur = sync + TABLES_AT + (gen & 1u) * TABLE;
+  u32* nxt = sync + TABLES_AT + (~gen & 1u) * TABLE;
+  int* tot = reinterpret_cast<int*>(cur);
+  int* chunk = tot + EXPERTS;
+  u32* bits = cur + EXPERTS * (1 + CHUNKS);
+  for (int i = gt; i < TABLE; i += nthreads) nxt[i] = 0u;  // the next call's table
+
+  // ---- phase 1a: a warp a row: top-16, marked in this call's table
+  const float rsv = __bfloat162float(rs[0]);
+  for (int b = gwarp; b < B; b += nwarps) {
+    const int e = topk_keys_warp<EXPERTS / 32>(S + (long long)b * EXPERTS, bias, TOPK, rsv, lane,
+                                               idx + (long long)b * TOPK, wts + (long long)b * TOPK);
+    if (lane < TOPK) {
+      atomicAdd(tot + e, 1);
+      atomicAdd(chunk + e * CHUNKS + b / CHUNK, 1);
+      atomicOr(bits + e * WORDS + b / 32, 1u << (b & 31));
+    }
+  }
+  // ---- phase 1b: 256-column pieces, a warp a piece: the latent's MXFP8 (kern_k3_moe_quant's bytes) and
+  // the shared expert's SiTU activation
+  const int nq = B * (LATENT / 256), ns = B * (SHARED_W / 256);
+  for (int i = gwarp; i < nq + ns; i += nwarps) {
+    if (i < nq) {
+      const int b = i / (LATENT / 256), c = (i % (LATENT / 256)) * 256 + lane * 8;
+      int sfb;
+      const uint2 w = quant8_lanes(*reinterpret_cast<const uint4*>(x + (long long)b * ldx + c), sfb);
+      *reinterpret_cast<uint2*>(q + (long long)b * LATENT + c) = w;
+      if ((lane & 3) == 0) sf[(long long)b * (LATENT / 32) + c / 32] = (uint8_t)sfb;
+    } else {
+      const int j = i - nq, b = j / (SHARED_W / 256), c = (j % (SHARED_W / 256)) * 256 + lane * 8;
+      const uint4 gv = *reinterpret_cast<const uint4*>(gu + (long long)b * ldgu + c);
+      const uint4 uv = *reinterpret_cast<const uint4*>(gu + (long long)b * ldgu + SHARED_W + c);
+      const u32* gp = reinterpret_cast<const u32*>(&gv);
+      const u32* up = reinterpret_cast<const u32*>(&uv);
+      uint4 o;
+      u32* op = reinterpret_cast<u32*>(&o);
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        const float2 g2 = bf16x2_to_f2(gp[l]), u2 = bf16x2_to_f2(up[l]);
+        op[l] = f2_to_bf16x2(situ_front(g2.x, u2.x), situ_front(g2.y, u2.y));
+      }
+      *reinterpret_cast<uint4*>(act + (long long)b * ldact + c) = o;
+    }
+  }
+
+  // ---- grid barrier (every block resident); a wait that runs out marks the error word and leaves
+  __syncthreads();
+  if (t == 0) {
+    __threadfence();
+    s_ok = 1u;
+    if (atomicAdd(sync + ARRIVE_AT, 1u) == gridDim.x - 1) {
+      atomicExch(sync + ARRIVE_AT, 0u);
+      __threadfence();
+      st_release_gpu(sync + GEN_AT, gen + 1u);
+    } else {
+      const u64 t0 = globaltimer_ns();
+      while (ld_acquire_gpu(sync + GEN_AT) == gen) {
+        if (globaltimer_ns() - t0 > BARRIER_LIMIT_NS) {
+          atomicOr(sync + ERR_AT, 1u);
+          s_ok = 0u;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  if (!s_ok) return;
+
+  // ---- phase 2: CTA counts of the experts exclusive-scanned (thread t: experts 2t and 2t + 1)
+  int c0 = 0, c1 = 0;
+  if (2 * t < EXPERTS) {
+    s_cnt[2 * t] = __ldcg(tot + 2 * t);
+    s_cnt[2 * t + 1] = __ldcg(tot + 2 * t + 1);
+    c0 = (s_cnt[2 * t] + tile - 1) / tile;
+    c1 = (s_cnt[2 * t + 1] + tile - 1) / tile;
+  }
+  int incl = c0 + c1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) s_wsum[warp] = incl;
+  __syncthreads();
+  int before = 0, total = 0;
+  for (int w = 0; w < RT_WARPS; ++w) {
+    before += w < warp ? s_wsum[w] : 0;
+    total += s_wsum[w];
+  }
+  if (2 * t < EXPERTS) {
+    s_off[2 * t] = before + incl - c0 - c1;
+    s_off[2 * t + 1] = before + incl - c1;
+  }
+  __syncthreads();
+  if (gt == 0) {
+    num_non_exiting[0] = total;
+    total_padded[0] = total * tile;
+  }
+  for (int e = gt; e < EXPERTS; e += nthreads) {
+    const int n = (s_cnt[e] + tile - 1) / tile, o = s_off[e];
+    for (int c = 0; c < n; ++c) {
+      cta_batch[o + c] = e;
+      cta_limit[o + c] = min((o + c + 1) * tile, o * tile + s_cnt[e]);
+    }
+  }
+  // a pick's place among its expert's rows: its picks in the chunks before the row's chunk, then in the
+  // chunk's bitmap words before the row's word, then in that word below the row (row order, every run alike)
+  for (int b = gwarp; b < B; b += nwarps) {
+    const int mine = lane < TOPK ? idx[(long long)b * TOPK + lane] : 0;
+    const int bc = b / CHUNK, bw = b / 32;
+    int place = 0;
+    for (int k = 0; k < TOPK; ++k) {
+      const int e = __shfl_sync(0xffffffffu, mine, k);
+      int v = lane < bc ? __ldcg(chunk + e * CHUNKS + lane) : 0;
+      const int w = bc * (CHUNK / 32) + lane;
+      if (w <= bw) {
+        const u32 word = __ldcg(bits + e * WORDS + w);
+        v += __popc(w < bw ? word : (word & ((1u << (b & 31)) - 1u)));
+      }
+      v = __reduce_add_sync(0xffffffffu, v);
+      if (lane == k) place = v;
+    }
+    if (lane < TOPK) {
+      const int p = s_off[mine] * tile + place;
+      exp2perm[(long long)b * TOPK + lane] = p;
+      route_map[p] = b;
+    }
+  }
+}
+
+// kern_k3g_moe_route_init (source/k3_moe_route.cu:522): zero the sync words before a stage's first call
+extern "C" __global__ void __launch_bounds__(1024) kern_k3g_moe_route_init(u32* __restrict__ sync) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dropin::SYNC_WORDS; i += gridDim.x * blockDim.x) sync[i] = 0u;
 }

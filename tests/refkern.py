@@ -23,6 +23,8 @@ def _drv():
         _cuda.cuLaunchKernel.argtypes = [ctypes.c_void_p] + [ctypes.c_uint] * 6 + [ctypes.c_uint, ctypes.c_void_p,
                                                                                   ctypes.POINTER(ctypes.c_void_p),
                                                                                   ctypes.c_void_p]
+        _cuda.cuLaunchCooperativeKernel.argtypes = [ctypes.c_void_p] + [ctypes.c_uint] * 6 + [
+            ctypes.c_uint, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
     return _cuda
 
 
@@ -57,6 +59,17 @@ def launch(f, grid, block, args, smem=0):
     rc = _drv().cuLaunchKernel(f, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem, s, arr, None)
     if rc != 0:
         raise RuntimeError(f"cuLaunchKernel = {rc}")
+
+
+def launch_cooperative(f, grid, block, args, smem=0):
+    """launch() as a cooperative launch: the driver starts every block at once or refuses the launch, so a
+    kernel whose blocks wait on one another (a grid barrier) cannot wait for a block that never starts."""
+    holders = [ctypes.pointer(a) for a in args]
+    arr = (ctypes.c_void_p * len(args))(*[ctypes.cast(h, ctypes.c_void_p) for h in holders])
+    s = torch.cuda.current_stream().cuda_stream
+    rc = _drv().cuLaunchCooperativeKernel(f, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem, s, arr)
+    if rc != 0:
+        raise RuntimeError(f"cuLaunchCooperativeKernel = {rc}")
 
 
 def P(t: torch.Tensor):

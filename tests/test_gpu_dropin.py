@@ -154,3 +154,56 @@ def test_finalize_rms(dev, T, rows):
 
     ro, o = _both("k3_moe_route", "kern_k3g_moe_finalize_rms", (rows, 1, 1), (cols // 8, 1, 1), mk_route)
     assert torch.equal(o.view(torch.int16), ro.view(torch.int16))
+
+
+# kern_k3g_moe_route's sync words (source/k3_moe_route.cu:317-333): barrier words, two routing tables, counters
+ROUTE_TABLE = E * (1 + 8192 // 256 + 8192 // 32)
+ROUTE_SYNC_WORDS = 64 + 2 * ROUTE_TABLE + 2
+SHARED_W = 6144
+
+
+@pytest.mark.parametrize("Bs", [(64, 200), (300, 2048)])
+def test_fused_route(dev, Bs):
+    """The fused prefill front, two calls in a row on one sync buffer (the second on the other parity's
+    table), each launched cooperatively so every block of the grid barrier is resident; all eleven outputs
+    byte-equal to the reference entry's."""
+    rng = np.random.default_rng(sum(Bs))
+    ldx, ldgu, ldact = LATENT + 64, 2 * SHARED_W + 128, SHARED_W + 64
+    bias = _t(rng.uniform(-0.1, 0.1, E).astype(np.float32), dev)
+    rs = _t(oracle.bf16_bits(np.array([2.5], np.float32)), dev).view(torch.bfloat16)
+    ins = []
+    for B in Bs:
+        S = _t(rng.standard_normal((B, E)).astype(np.float32), dev)
+        x = _t(oracle.bf16_bits(rng.standard_normal((B, ldx)).astype(np.float32)), dev).view(torch.bfloat16)
+        gu = _t(oracle.bf16_bits((3.0 * rng.standard_normal((B, ldgu))).astype(np.float32)), dev).view(torch.bfloat16)
+        ins.append((B, S, x, gu))
+
+    def run(module):
+        f_init = rk.function(module, "kern_k3g_moe_route_init")
+        f = rk.function(module, "kern_k3g_moe_route")
+        sync = _poison((ROUTE_SYNC_WORDS,), torch.int32, dev)
+        rk.launch(f_init, (64, 1, 1), (1024, 1, 1), [rk.P(sync)])
+        outs = []
+        for B, S, x, gu in ins:
+            ctas = E + (B * TOPK + 127) // 128
+            o = dict(q=_poison((B, LATENT), torch.uint8, dev), sf=_poison((B, LATENT // 32), torch.uint8, dev),
+                     idx=_poison((B, TOPK), torch.int32, dev), wts=_poison((B, TOPK), torch.float32, dev),
+                     act=_poison((B, ldact), torch.bfloat16, dev), cta_batch=_poison((ctas,), torch.int32, dev),
+                     cta_limit=_poison((ctas,), torch.int32, dev), nne=_poison((1,), torch.int32, dev),
+                     tp=_poison((1,), torch.int32, dev), route_map=_poison((ctas * 128,), torch.int32, dev),
+                     exp2perm=_poison((B, TOPK), torch.int32, dev))
+            args = [rk.P(S), rk.P(bias), rk.P(rs), rk.P(x), rk.I(ldx), rk.P(gu), rk.I(ldgu), rk.P(o["q"]),
+                    rk.P(o["sf"]), rk.P(o["idx"]), rk.P(o["wts"]), rk.P(o["act"]), rk.I(ldact), rk.P(sync),
+                    rk.P(o["cta_batch"]), rk.P(o["cta_limit"]), rk.P(o["nne"]), rk.P(o["tp"]), rk.P(o["route_map"]),
+                    rk.P(o["exp2perm"]), rk.I(128), rk.I(B)]
+            rk.launch_cooperative(f, (64 if B <= 256 else 288, 1, 1), (512, 1, 1), args)
+            torch.cuda.synchronize()
+            outs.append(o)
+        return outs, sync
+
+    ref, _ = run("k3_moe_route")
+    got, sync = run(MOD)
+    assert int(sync[1].item()) == 0, "a grid-barrier wait ran out"
+    for call, (r, g) in enumerate(zip(ref, got)):
+        for name in r:
+            assert torch.equal(r[name].view(torch.uint8), g[name].view(torch.uint8)), f"call {call}: {name} differs"
