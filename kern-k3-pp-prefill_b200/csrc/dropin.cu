@@ -2,7 +2,7 @@
 // and launch geometry (docs/k3-kernel-abi.md §0 conventions; kernels.toml), so
 // a manifest that binds the reference's modules can bind this one instead.
 // Every entry computes with this project's own kernels' arithmetic and matches
-// the reference entry byte for byte (tests/test_gpu_ref.py).  TOPK is 16 and
+// the reference entry byte for byte (tests/test_gpu_dropin.py).  TOPK is 16 and
 // LATENT 3584, as compiled into the reference modules.
 //
 //   kern_k3_moe_quant           source/k3_moe_prefill.cu:66   grid ceil(rows*cols/32/256), block 256
@@ -16,6 +16,8 @@
 //   kern_k3g_moe_finalize_rms   source/k3_moe_route.cu:538    grid rows, block 448
 //   kern_k3g_moe_route          source/k3_moe_route.cu:338    grid 64 (B <= 256) or 288, block 512 (grid barrier)
 //   kern_k3g_moe_route_init     source/k3_moe_route.cu:522    any grid, block 1024
+//   kern_k3_moe_w_shuffle       source/k3_moe_prefill.cu:242  grid ceil(experts*n*row_bytes/16/block)
+//   kern_k3_moe_sf_shuffle      source/k3_moe_prefill.cu:252  grid ceil(experts*n*kg/block)
 #include "common.cuh"
 
 namespace k3 {
@@ -519,4 +521,41 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
 // kern_k3g_moe_route_init (source/k3_moe_route.cu:522): zero the sync words before a stage's first call
 extern "C" __global__ void __launch_bounds__(1024) kern_k3g_moe_route_init(u32* __restrict__ sync) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dropin::SYNC_WORDS; i += gridDim.x * blockDim.x) sync[i] = 0u;
+}
+
+// ------------------------------------------------------------------ load-time weight re-layouts
+// kern_k3_moe_w_shuffle / kern_k3_moe_sf_shuffle (source/k3_moe_prefill.cu:237-259, registered by
+// scripts/k3_moe_bmm.py:176-184): the checkpoint's expert rows into the row order the TRT-LLM-gen GEMMs'
+// epilogue expects, and (sf) the row scales into the 128x4-tiled layout.  Within each 32-row group, GEMM
+// row r takes the checkpoint row whose position is (r % 8) * 4 + (r % 32) / 8 (a transpose of the 8 x 4
+// arrangement); `gated` interleaves the two halves [up | gate] of FC1's 2I rows, even positions from the
+// first half, odd from the second.  The layout is the consumer's (the prebuilt GEMMs), so the map is fixed.
+__device__ __forceinline__ int gemm_row_source(int r, int n, int gated) {
+  const int pos = (r & ~31) + (r & 7) * 4 + ((r & 31) >> 3);
+  if (!gated) return pos;
+  return (pos & 1) * (n / 2) + (pos >> 1);
+}
+
+// grid ceil(experts * n * row_bytes / 16 / block), any block: one 16-byte chunk a thread
+extern "C" __global__ void kern_k3_moe_w_shuffle(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                 int experts, int n, int row_bytes, int gated) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int chunks = row_bytes / 16;
+  if (i >= (long long)experts * n * chunks) return;
+  const long long row = i / chunks;  // expert * n + r
+  const int c = (int)(i - row * chunks);
+  const int e = (int)(row / n), r = (int)(row - (long long)e * n);
+  const uint4* s = reinterpret_cast<const uint4*>(src + ((long long)e * n + gemm_row_source(r, n, gated)) * row_bytes);
+  reinterpret_cast<uint4*>(dst)[i] = s[c];
+}
+
+// grid ceil(experts * n * kg / block), any block: one scale byte a thread (kg = K / 32 groups a row)
+extern "C" __global__ void kern_k3_moe_sf_shuffle(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                  int experts, int n, int kg, int gated) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)experts * n * kg) return;
+  const long long row = i / kg;
+  const int c = (int)(i - row * kg);
+  const int e = (int)(row / n), r = (int)(row - (long long)e * n);
+  dst[(long long)e * n * kg + sf_tiled_offset(r, c, kg / 4)] = src[((long long)e * n + gemm_row_source(r, n, gated)) * kg + c];
 }

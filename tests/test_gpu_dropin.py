@@ -207,3 +207,28 @@ def test_fused_route(dev, Bs):
     for call, (r, g) in enumerate(zip(ref, got)):
         for name in r:
             assert torch.equal(r[name].view(torch.uint8), g[name].view(torch.uint8)), f"call {call}: {name} differs"
+
+
+@pytest.mark.parametrize("experts,n,K,gated", [(3, 256, 3584, 1), (2, 7168, 512, 0), (1, 64, 256, 1)])
+def test_weight_shuffles(dev, experts, n, K, gated):
+    """The load-time re-layouts of the checkpoint's MXFP4 rows (packed bytes) and their scales."""
+    rng = np.random.default_rng(experts * n + K)
+    row_bytes, kg = K // 2, K // 32
+    w = _t(rng.integers(0, 256, (experts * n, row_bytes), dtype=np.uint8), dev)
+    s = _t(rng.integers(0, 256, (experts * n, kg), dtype=np.uint8), dev)
+
+    def mk_w():
+        out = _poison((experts * n, row_bytes), torch.uint8, dev)
+        return [rk.P(w), rk.P(out), rk.I(experts), rk.I(n), rk.I(row_bytes), rk.I(gated)], out
+
+    total = experts * n * row_bytes // 16
+    ro, o = _both("k3_moe_prefill", "kern_k3_moe_w_shuffle", ((total + 255) // 256, 1, 1), (256, 1, 1), mk_w)
+    assert torch.equal(o, ro)
+
+    def mk_sf():
+        out = _poison((experts * n * kg,), torch.uint8, dev)
+        return [rk.P(s), rk.P(out), rk.I(experts), rk.I(n), rk.I(kg), rk.I(gated)], out
+
+    total = experts * n * kg
+    ro, o = _both("k3_moe_prefill", "kern_k3_moe_sf_shuffle", ((total + 255) // 256, 1, 1), (256, 1, 1), mk_sf)
+    assert torch.equal(o, ro)
