@@ -87,11 +87,13 @@ extern "C" __global__ void __launch_bounds__(128) kern_k3g_router_topk(const flo
                                                                        const bf16* __restrict__ rs,
                                                                        int* __restrict__ idx, float* __restrict__ wts,
                                                                        int B) {
-  const int b = blockIdx.x * 4 + (threadIdx.x >> 5);
+  __shared__ u32 ck[4][TOPK_CAND];
+  __shared__ int ce[4][TOPK_CAND];
+  const int warp = threadIdx.x >> 5, b = blockIdx.x * 4 + warp;
   if (b >= B) return;
   topk_warp<dropin::EXPERTS / 32>(S + (long long)b * dropin::EXPERTS, bias, dropin::EXPERTS, dropin::TOPK,
-                                  __bfloat162float(rs[0]), threadIdx.x & 31, idx + (long long)b * dropin::TOPK,
-                                  wts + (long long)b * dropin::TOPK);
+                                  __bfloat162float(rs[0]), threadIdx.x & 31, ck[warp], ce[warp],
+                                  idx + (long long)b * dropin::TOPK, wts + (long long)b * dropin::TOPK);
 }
 
 // ------------------------------------------------------------------ EP-slice routing tables (top-16)
@@ -326,45 +328,6 @@ __device__ __forceinline__ float situ_front(float g, float u) {
   return __fmul_rn(__fmul_rn(a, __frcp_rn(d)), c);
 }
 
-// One warp a row: keys ord(sigmoid(S) + bias) of experts j*32 + lane, the K largest (ties to the smaller
-// expert), lane r < K ending with the r-th pick; its weight is the pick's sigmoid over the picks' butterfly
-// sum, times rs: kern_k3g_router_topk's values (topk_warp) with the keys alone held in registers.
-template <int EPL>
-__device__ __forceinline__ int topk_keys_warp(const float* __restrict__ row, const float* __restrict__ bias, int K,
-                                              float rsv, int lane, int* __restrict__ idx_out,
-                                              float* __restrict__ wts_out) {
-  u32 o[EPL];
-#pragma unroll
-  for (int j = 0; j < EPL; ++j) {
-    const int e = j * 32 + lane;
-    o[j] = ord_f32(1.0f / (1.0f + expf(-row[e])) + bias[e]);
-  }
-  int pick = 0;
-  for (int r = 0; r < K; ++r) {
-    u32 m = o[0];
-#pragma unroll
-    for (int j = 1; j < EPL; ++j) m = max(m, o[j]);
-    m = __reduce_max_sync(0xffffffffu, m);
-    u32 mine = 0xffffffffu;
-#pragma unroll
-    for (int j = EPL - 1; j >= 0; --j)
-      if (o[j] == m) mine = (u32)(j * 32 + lane);
-    const u32 ew = __reduce_min_sync(0xffffffffu, mine);
-#pragma unroll
-    for (int j = 0; j < EPL; ++j)
-      if (j * 32 + lane == (int)ew) o[j] = 0u;
-    if (lane == r) pick = (int)ew;
-  }
-  const float w = lane < K ? 1.0f / (1.0f + expf(-row[pick])) : 0.f;
-  float den = w;
-  for (int off = K / 2; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-  if (lane < K) {
-    wts_out[lane] = (w / (den + 1e-20f)) * rsv;
-    idx_out[lane] = pick;
-  }
-  return pick;
-}
-
 }  // namespace k3
 
 extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe_route(
@@ -378,6 +341,8 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
   __shared__ u32 s_gen, s_ok;
   __shared__ int s_cnt[EXPERTS], s_off[EXPERTS];
   __shared__ int s_wsum[RT_WARPS];
+  __shared__ u32 s_ck[RT_WARPS][TOPK_CAND];
+  __shared__ int s_ce[RT_WARPS][TOPK_CAND];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int nthreads = gridDim.x * RT_THREADS, gt = blockIdx.x * RT_THREADS + t;
   const int gwarp = blockIdx.x * RT_WARPS + warp, nwarps = gridDim.x * RT_WARPS;
@@ -396,8 +361,8 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
   // ---- phase 1a: a warp a row: top-16, marked in this call's table
   const float rsv = __bfloat162float(rs[0]);
   for (int b = gwarp; b < B; b += nwarps) {
-    const int e = topk_keys_warp<EXPERTS / 32>(S + (long long)b * EXPERTS, bias, TOPK, rsv, lane,
-                                               idx + (long long)b * TOPK, wts + (long long)b * TOPK);
+    const int e = topk_warp<EXPERTS / 32>(S + (long long)b * EXPERTS, bias, EXPERTS, TOPK, rsv, lane, s_ck[warp],
+                                          s_ce[warp], idx + (long long)b * TOPK, wts + (long long)b * TOPK);
     if (lane < TOPK) {
       atomicAdd(tot + e, 1);
       atomicAdd(chunk + e * CHUNKS + b / CHUNK, 1);

@@ -14,74 +14,128 @@
 namespace k3 {
 
 // ============================================================ router top-k
-// One warp a row.  Lane l holds experts e = j*32 + l.  sig = 1/(1+expf(-s)),
-// key = ord(sig + bias); K rounds each take the largest remaining key and the
-// smallest expert holding it (ties -> smaller e), lane r keeping round r's
-// pick.  Weights: sig / (butterfly sum over the K picks + 1e-20) * rs.
-// K must be a power of two <= 16 (the butterfly pairs lanes r ^ o, o < K).
+// One warp a row.  Lane l holds experts e = j*32 + l: key = ord(sig + bias), sig = 1/(1+expf(-s)) (an
+// IEEE reciprocal).  The K largest keys, ties to the smaller expert, lane r ending with the r-th pick;
+// weights sig / (butterfly sum over the K picks + 1e-20) * rs.  K must be a power of two <= 16.
+//
+// Selection: tau = the K-th largest of the 32 lane maxima (a bitonic sort across the warp) bounds the
+// K-th largest key from below (K lanes hold a key >= tau), so only keys >= tau are candidates; they are
+// compacted into shared memory and each ranked by counting the candidates ahead of it.  With more than
+// TOPK_CAND candidates (ties on a large scale), K rounds of warp max / min over the registers instead.
 #define TOPK_MAX_EPL 32  // experts per lane: E <= 1024
+#define TOPK_CAND 64     // candidate slots a warp (shared memory)
 
+__device__ __forceinline__ float router_sigmoid(float s) { return __frcp_rn(1.0f + expf(-s)); }
+
+// Returns this lane's pick (lanes < K).
 template <int EPL>
-__device__ __forceinline__ void topk_warp(const float* __restrict__ row, const float* __restrict__ bias, int E, int K,
-                                          float rsv, int lane, int* __restrict__ idx_out, float* __restrict__ wts_out) {
+__device__ __forceinline__ int topk_warp(const float* __restrict__ row, const float* __restrict__ bias, int E, int K,
+                                         float rsv, int lane, u32* __restrict__ ck, int* __restrict__ ce,
+                                         int* __restrict__ idx_out, float* __restrict__ wts_out) {
   u32 o[EPL];
-  float g[EPL];
 #pragma unroll
   for (int j = 0; j < EPL; ++j) {
     const int e = j * 32 + lane;
-    if (e < E) {
-      const float sg = 1.0f / (1.0f + expf(-row[e]));
-      g[j] = sg;
-      o[j] = ord_f32(sg + bias[e]);
-    } else {
-      g[j] = 0.f;
-      o[j] = 0u;  // below the key of every finite float
-    }
+    o[j] = e < E ? ord_f32(router_sigmoid(row[e]) + bias[e]) : 0u;  // 0: below every real key
   }
-  float pick_w = 0.f;
-  int pick_e = 0;
-  for (int r = 0; r < K; ++r) {
-    u32 m = o[0];
+  // tau: bitonic sort of the lane maxima, descending; lane K-1 holds the K-th largest
+  u32 v = o[0];
 #pragma unroll
-    for (int j = 1; j < EPL; ++j) m = max(m, o[j]);
-    m = __reduce_max_sync(0xffffffffu, m);
-    u32 my = 0xffffffffu;
+  for (int j = 1; j < EPL; ++j) v = max(v, o[j]);
 #pragma unroll
-    for (int j = EPL - 1; j >= 0; --j)
-      if (o[j] == m) my = (u32)(j * 32 + lane);
-    const u32 ew = __reduce_min_sync(0xffffffffu, my);
-    float gw = 0.f;
-    if (my == ew) {
+  for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const u32 p = __shfl_xor_sync(0xffffffffu, v, j);
+      const bool up = ((lane & k) == 0) == ((lane & j) == 0);  // keep the larger in the lower lane of a pair
+      v = up ? max(v, p) : min(v, p);
+    }
+  const u32 tau = __shfl_sync(0xffffffffu, v, K - 1);
+  int c = 0;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) c += o[j] >= tau;
+  int incl = c;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  const int n = __shfl_sync(0xffffffffu, incl, 31);
+  int pick = 0;
+  if (n <= TOPK_CAND) {
+    int at = incl - c;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (o[j] >= tau) {
+        ck[at] = o[j];
+        ce[at] = j * 32 + lane;
+        ++at;
+      }
+    __syncwarp();
+    // candidate i's rank: the candidates with a larger key, or the same key and a smaller expert
+    int rk[TOPK_CAND / 32], ex[TOPK_CAND / 32];
+#pragma unroll
+    for (int h = 0; h < TOPK_CAND / 32; ++h) {
+      const int i = lane + 32 * h;
+      rk[h] = K;
+      if (i < n) {
+        const u32 ki = ck[i];
+        const int ei = ce[i];
+        int r = 0;
+        for (int q = 0; q < n; ++q) {
+          const u32 kq = ck[q];
+          r += (kq > ki) | ((kq == ki) & (ce[q] < ei));
+        }
+        rk[h] = r;
+        ex[h] = ei;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < TOPK_CAND / 32; ++h)
+      if (rk[h] < K) ce[rk[h]] = ex[h];
+    __syncwarp();
+    if (lane < K) pick = ce[lane];
+    __syncwarp();
+  } else {
+    for (int r = 0; r < K; ++r) {
+      u32 m = o[0];
+#pragma unroll
+      for (int j = 1; j < EPL; ++j) m = max(m, o[j]);
+      m = __reduce_max_sync(0xffffffffu, m);
+      u32 mine = 0xffffffffu;
+#pragma unroll
+      for (int j = EPL - 1; j >= 0; --j)
+        if (o[j] == m) mine = (u32)(j * 32 + lane);
+      const u32 ew = __reduce_min_sync(0xffffffffu, mine);
 #pragma unroll
       for (int j = 0; j < EPL; ++j)
-        if (j * 32 + lane == (int)ew) {
-          gw = g[j];
-          o[j] = 0u;
-        }
-    }
-    gw = __shfl_sync(0xffffffffu, gw, (int)(ew & 31u));
-    if (lane == r) {
-      pick_w = gw;
-      pick_e = (int)ew;
+        if (j * 32 + lane == (int)ew) o[j] = 0u;
+      if (lane == r) pick = (int)ew;
     }
   }
-  float den = pick_w;
+  const float w = lane < K ? router_sigmoid(row[pick]) : 0.f;
+  float den = w;
   for (int off = K / 2; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
   if (lane < K) {
-    wts_out[lane] = (pick_w / (den + 1e-20f)) * rsv;
-    idx_out[lane] = pick_e;
+    wts_out[lane] = (w / (den + 1e-20f)) * rsv;
+    idx_out[lane] = pick;
   }
+  return pick;
 }
 
 template <int EPL>
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ S, int lds, const float* __restrict__ bias,
                                                    const bf16* __restrict__ rs, int T, int E, int K,
                                                    int* __restrict__ idx, float* __restrict__ wts) {
-  const int lane = threadIdx.x & 31;
+  __shared__ u32 ck[8][TOPK_CAND];
+  __shared__ int ce[8][TOPK_CAND];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int warps = blockDim.x >> 5;
   const float rsv = __bfloat162float(rs[0]);
-  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps)
-    topk_warp<EPL>(S + (long long)t * lds, bias, E, K, rsv, lane, idx + (long long)t * K, wts + (long long)t * K);
+  for (int t = blockIdx.x * warps + warp; t < T; t += gridDim.x * warps)
+    topk_warp<EPL>(S + (long long)t * lds, bias, E, K, rsv, lane, ck[warp], ce[warp], idx + (long long)t * K,
+                   wts + (long long)t * K);
 }
 
 // ============================================================ routing tables
