@@ -234,7 +234,7 @@ int k3moe_route_tables(const int32_t* idx, int R, int K, int first, int E, int s
                                          route_map);
   const int sc_smem = E * (TB / 32) * 4;
   if (sc_smem > 48 * 1024 && !set_smem_once(route_scatter_kernel, sc_smem, 2)) return K3MOE_ELAUNCH;
-  route_scatter_kernel<<<nb, TB, sc_smem, s>>>(idx, R, K, first, E, shared, blockoff, route_map, exp2perm);
+  route_scatter_kernel<<<nb, TB, sc_smem, s>>>(idx, R, K, first, E, shared, blockcount, blockoff, route_map, exp2perm);
   return launch_status();
 }
 

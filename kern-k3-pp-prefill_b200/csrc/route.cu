@@ -170,10 +170,10 @@ __global__ void __launch_bounds__(TB) route_count_kernel(const int* __restrict__
 // ceil(count/tile) exclusive-scanned into off[e]; cta c of expert e covers
 // permuted rows [tile*c, tile*(c+1)), real up to cta_limit[c] =
 // min(tile*(c+1), tile*off[e] + count[e]); padding rows route row 0.
-// blockoff[b][e] = tile*off[e] + picks of e in the blocks before b.
+// blockoff[b][e] = picks of e in the blocks before b; blockcount[0][e] (read, then reused) = tile*off[e].
 // meta[0] = num_non_exiting, meta[1] = total_padded, meta[2] = the shared
 // expert's first permuted row (tile*off[E]) or -1.
-__global__ void __launch_bounds__(1024) route_tables_kernel(const int* __restrict__ blockcount, int blocks, int E,
+__global__ void __launch_bounds__(1024) route_tables_kernel(int* __restrict__ blockcount, int blocks, int E,
                                                              int shared, int tile, int* __restrict__ blockoff,
                                                              int* __restrict__ counts, int* __restrict__ cta_batch,
                                                              int* __restrict__ cta_limit, int* __restrict__ meta,
@@ -183,9 +183,20 @@ __global__ void __launch_bounds__(1024) route_tables_kernel(const int* __restric
   __shared__ int s_wsum[32];
   const int EL = E + shared;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  // an expert's picks before each block (its column of blockcount, loads 8 at a time so they overlap)
   for (int e = t; e < EL; e += blockDim.x) {
-    int run = 0;
-    for (int b = 0; b < blocks; ++b) {
+    int run = 0, b = 0;
+    for (; b + 8 <= blocks; b += 8) {
+      int c[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) c[i] = blockcount[(long long)(b + i) * EL + e];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        blockoff[(long long)(b + i) * EL + e] = run;
+        run += c[i];
+      }
+    }
+    for (; b < blocks; ++b) {
       const int c = blockcount[(long long)b * EL + e];
       blockoff[(long long)b * EL + e] = run;
       run += c;
@@ -229,15 +240,17 @@ __global__ void __launch_bounds__(1024) route_tables_kernel(const int* __restric
       cta_limit[o + c] = min((o + c + 1) * tile, o * tile + cnt);
     }
     for (int r = o * tile + cnt; r < (o + n) * tile; ++r) route_map[r] = 0;
-    for (int b = 0; b < blocks; ++b) blockoff[(long long)b * EL + e] += o * tile;
+    // the expert's first permuted row, for the scatter: row 0 of blockcount is spent, its column e is reused
+    blockcount[e] = o * tile;
   }
 }
 
-// The permuted row of pick (r, k) is blockoff[b][e] + the picks of e by rows of
-// the block before r (a bitmap popcount): route_map[row] = r, exp2perm[r*K+k] = row.
+// The permuted row of pick (r, k) is ebase[e] (the expert's first row) + blockoff[b][e] + the picks of e
+// by rows of the block before r (a bitmap popcount): route_map[row] = r, exp2perm[r*K+k] = row.
 // Shared-expert rows are tile*off[E] + r and go to route_map only.
 __global__ void __launch_bounds__(TB) route_scatter_kernel(const int* __restrict__ ids, int R, int K, int first, int E,
-                                                            int shared, const int* __restrict__ blockoff,
+                                                            int shared, const int* __restrict__ ebase,
+                                                            const int* __restrict__ blockoff,
                                                             int* __restrict__ route_map, int* __restrict__ exp2perm) {
   extern __shared__ u32 bits[];  // [E][TB/32]
   const int EL = E + shared;
@@ -265,12 +278,12 @@ __global__ void __launch_bounds__(TB) route_scatter_kernel(const int* __restrict
     int rank = 0;
     for (int w = 0; w < (lr >> 5); ++w) rank += __popc(bits[e * W + w]);
     rank += __popc(bits[e * W + (lr >> 5)] & ((1u << (lr & 31)) - 1u));
-    const int row = blockoff[(long long)blockIdx.x * EL + e] + rank;
+    const int row = ebase[e] + blockoff[(long long)blockIdx.x * EL + e] + rank;
     exp2perm[gi] = row;
     route_map[row] = r0 + lr;
   }
   if (shared) {
-    const int sb = blockoff[(long long)blockIdx.x * EL + E];
+    const int sb = ebase[E] + blockoff[(long long)blockIdx.x * EL + E];
     for (int lr = threadIdx.x; lr < nrows; lr += blockDim.x) route_map[sb + lr] = r0 + lr;
   }
 }
@@ -310,20 +323,29 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restri
                                                             uint8_t* __restrict__ sfp) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
-  const int kg4 = (cols / 32 + 3) / 4;
+  const int kt = cols / 128, kg4 = (cols / 32 + 3) / 4;
   const int shared_base = meta[2];
+  const int nd = K + (shared_base >= 0 ? 1 : 0);  // destination slots: the K picks, then the shared expert's row
   for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < R; r += gridDim.x * warps) {
-    int dst[17];
-    int nd = 0;
-    for (int k = 0; k < K; ++k) {
-      const int p = exp2perm[(long long)r * K + k];
-      if (p >= 0) dst[nd++] = p;
-    }
-    if (shared_base >= 0) dst[nd++] = shared_base + r;
+    // lane d < nd holds destination d's permuted row (or -1) and its row bases in q and in the scales
+    int p = -1;
+    if (lane < K) p = exp2perm[(long long)r * K + lane];
+    else if (lane == K && shared_base >= 0) p = shared_base + r;
+    const long long qrow = p >= 0 ? (long long)(p >> 7) * kt * (128 * 128) + (p & 127) * 128 : 0;
+    const long long srow = p >= 0 ? (long long)(p >> 7) * kg4 * 512 + (p & 31) * 16 + ((p & 127) >> 5) * 4 : 0;
     const bf16* xr = x + (long long)r * ldx;
-    for (int c0 = 0; c0 < cols; c0 += 256) {
+    // the row's pieces four at a time: their loads in flight together
+    for (int c00 = 0; c00 < cols; c00 += 4 * 256) {
+      uint4 ub[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (c00 + i * 256 < cols) ub[i] = *reinterpret_cast<const uint4*>(xr + c00 + i * 256 + lane * 8);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+      const int c0 = c00 + i * 256;
+      if (c0 >= cols) break;
       const int c = c0 + lane * 8;
-      const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+      const uint4 u = ub[i];
       int sfb;
       const uint2 w = quant8_lanes(u, sfb);
       // gather the 4 groups' scale bytes of this 128-column half into lane 0 / 16
@@ -331,10 +353,16 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restri
       u32 sfw = (u32)sfb << (8 * (kb & 3));
       sfw |= __shfl_down_sync(0xffffffffu, sfw, 4);
       sfw |= __shfl_down_sync(0xffffffffu, sfw, 8);
+      const int qcol = (c >> 7) * (128 * 128) + (c & 127);
+      const int scol = (kb >> 2) * 512;
       for (int d = 0; d < nd; ++d) {
-        const long long p = dst[d];
-        *reinterpret_cast<uint2*>(qp + op8_offset(p, c, cols)) = w;
-        if ((lane & 15) == 0) *reinterpret_cast<u32*>(sfp + sf_tiled_offset(p, kb, kg4)) = sfw;
+        const int pd = __shfl_sync(0xffffffffu, p, d);
+        if (pd < 0) continue;  // the same for the whole warp
+        const long long qd = __shfl_sync(0xffffffffu, qrow, d);
+        const long long sd = __shfl_sync(0xffffffffu, srow, d);
+        *reinterpret_cast<uint2*>(qp + qd + qcol) = w;
+        if ((lane & 15) == 0) *reinterpret_cast<u32*>(sfp + sd + scol) = sfw;
+      }
       }
     }
   }
