@@ -393,9 +393,12 @@ int k3moe_ep_pack(const void* x_bf16, int ldx, int T, int H, int K, const int32_
       (send_pos && (K < 1 || K > 16 || !idx || E_local < 1)))
     return K3MOE_EINVAL;
   if (T == 0) return K3MOE_OK;
-  const int grid = (int)std::min<long long>(cdiv(T, 8), (long long)num_sms(current_device()) * 8);
+  // several warps a row when there are few rows (a decode step): about four warps an SM in all
+  const int sms = num_sms(current_device());
+  const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
+  const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
   ep_pack_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, idx, send_pos, E_local, fixed_eid, dst, stride);
+      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, idx, send_pos, E_local, fixed_eid, dst, stride, split);
   return launch_status();
 }
 

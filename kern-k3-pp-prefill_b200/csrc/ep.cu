@@ -13,16 +13,19 @@
 
 namespace k3 {
 
-// One warp a source row: quantise it once and write it to each of its
-// destination slots: slot send_pos[t*K + k] with id idx[t*K + k] - dest*E_local
-// (dest = idx / E_local), or, with send_pos null, slot t with id `fixed_eid`.
+// `split` warps a source row, each a contiguous share of its 256-column pieces: quantise the row once and
+// write it to each of its destination slots: slot send_pos[t*K + k] with id idx[t*K + k] - dest*E_local
+// (dest = idx / E_local), or, with send_pos null, slot t with id `fixed_eid`.  (A decode step has a few
+// dozen rows: several warps a row keep more of the GPU busy.)
 __global__ void __launch_bounds__(256) ep_pack_kernel(const bf16* __restrict__ x, int ldx, int T, int H, int K,
                                                       const int* __restrict__ idx, const int* __restrict__ send_pos,
                                                       int E_local, int fixed_eid, uint8_t* __restrict__ dst,
-                                                      int stride) {
+                                                      int stride, int split) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
-  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
+  const int pieces = H / 256, share = (pieces + split - 1) / split;
+  for (int g = blockIdx.x * warps + (threadIdx.x >> 5); g < T * split; g += gridDim.x * warps) {
+    const int t = g / split, part = g - t * split;
     long long pos[16];
     int eid[16];
     int nd = 0;
@@ -41,7 +44,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const bf16* __restrict__ x
       nd = 1;
     }
     const bf16* xr = x + (long long)t * ldx;
-    for (int c0 = 0; c0 < H; c0 += 256) {
+    const int c_end = min(H, (part + 1) * share * 256);
+    for (int c0 = part * share * 256; c0 < c_end; c0 += 256) {
       const int c = c0 + lane * 8;
       const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
       int sfb;
@@ -56,7 +60,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const bf16* __restrict__ x
         if ((lane & 15) == 0) *reinterpret_cast<u32*>(row + H + kb) = sfw;
       }
     }
-    if (lane < nd) *reinterpret_cast<int*>(dst + pos[lane] * stride + H + H / 32) = eid[lane];
+    if (part == 0 && lane < nd) *reinterpret_cast<int*>(dst + pos[lane] * stride + H + H / 32) = eid[lane];
   }
 }
 

@@ -72,8 +72,9 @@ class GpuOps:
         return ids
 
     def unpack(self, rows, R, H, tb):
+        # rows past a tile's real rows are never read into a result: no need to clear either buffer
         qp = torch.empty((tb.cap_rows, H), dtype=torch.uint8, device=rows.device)
-        sfp = torch.zeros(tb.cap_rows * H // 32, dtype=torch.uint8, device=rows.device)
+        sfp = torch.empty(tb.cap_rows * H // 32, dtype=torch.uint8, device=rows.device)
         k3moe._check(k3moe.lib().k3moe_ep_unpack(rows.data_ptr(), rows.shape[1], R, H, tb.exp2perm.data_ptr(),
                                                  qp.data_ptr(), sfp.data_ptr(), k3moe._stream()), "ep_unpack")
         return qp, sfp
