@@ -104,7 +104,7 @@ def _worker(rank, world, port, outdir, mode):
 @pytest.mark.parametrize("mode", ["counts", "fixed", "graph"])
 def test_ep2_nccl_bit_identical_to_one_gpu(mode):
     if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs (run with gpurun --gpus 2)")
+        pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
