@@ -273,23 +273,43 @@ def e2e_overlapped(fwd, S_h, x_h, out_shape, steps, stream, dev):
     return e0.elapsed_time(e1) / steps
 
 
-def rank_weights(E, El, e0, dev):
-    """Experts [e0, e0 + El) then the shared expert, from the same synthetic stream as the full set."""
+def rank_weights(E, experts, dev):
+    """The listed routed experts (in order) then the shared expert, from the same synthetic stream as the full
+    set (every expert's rows are synthesised from their global row index)."""
     import torch
 
     import k3moe
 
+    El = len(experts)
     w = {}
     for name, rows_per, K_, seed in (("w13", 2 * I, H, W_SEED13), ("w2", H, I, W_SEED2)):
         packed = torch.empty(((El + SHARED) * rows_per, K_ // 2), dtype=torch.uint8, device=dev)
         sf = torch.zeros((El + SHARED) * rows_per // 128 * (K_ // 128) * 512, dtype=torch.uint8, device=dev)
         per_sf = rows_per // 128 * (K_ // 128) * 512
-        k3moe.synth_mxfp4(seed, El * rows_per, K_, WSD, row0=e0 * rows_per, packed=packed[:El * rows_per],
-                          sf=sf[:El * per_sf])
-        k3moe.synth_mxfp4(seed, rows_per, K_, WSD, row0=E * rows_per, packed=packed[El * rows_per:],
-                          sf=sf[El * per_sf:])
+        # runs of consecutive experts in one synthesis call each
+        runs, i = [], 0
+        while i < El:
+            j = i + 1
+            while j < El and experts[j] == experts[j - 1] + 1:
+                j += 1
+            runs.append((i, experts[i], j - i))
+            i = j
+        for at, e0, n in runs + ([(El, E, 1)] if SHARED else []):
+            k3moe.synth_mxfp4(seed, n * rows_per, K_, WSD, row0=e0 * rows_per,
+                              packed=packed[at * rows_per:(at + n) * rows_per], sf=sf[at * per_sf:(at + n) * per_sf])
         w[name], w[name + "_sf"] = packed, sf
     return w
+
+
+def rank_experts(E, world, rank, bias, placement):
+    """(owner [E] or None, this rank's experts in id order) for the placement policy."""
+    import k3moe_ep
+
+    if placement == "contiguous":
+        El = E // world
+        return None, list(range(rank * El, (rank + 1) * El))
+    owner = k3moe_ep.balanced_owner(bias, world)
+    return owner, (owner == rank).nonzero().flatten().tolist()
 
 
 def rank_inputs(T, E, rank, dev):
@@ -320,9 +340,10 @@ def run_ep(args, world, rank, dev):
 
     E, T = args.experts, args.tokens
     El = E // world
-    w = rank_weights(E, El, rank * El, dev)
     x, S, bias, rs = rank_inputs(T, E, rank, dev)
-    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev)
+    owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
+    w = rank_weights(E, mine, dev)
+    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, owner=owner)
     for _ in range(args.warmup):
         layer.forward(S, x)
     torch.cuda.synchronize()
@@ -369,6 +390,7 @@ def run_ep(args, world, rank, dev):
             "config": {"workload": f"K3-shape prefill MoE layer, expert parallel over {world} GPUs (config 4 layout)",
                        "T_per_gpu": T, "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I,
                        "rs": RS, "global_batch": T * world, "seq_len": T, "parallelism": f"ep{world}",
+                       "expert_placement": args.ep_placement,
                        "l2": "inputs larger than L2: each GPU streams its experts' weights every step"},
             "tflops": flops / (ms / 1e3) / 1e12,
             "a2a_ms": {"dispatch": disp_ms, "combine": comb_ms},
@@ -417,8 +439,9 @@ def run_decode(args, world, rank, dev):
         run = lambda: layer.forward(S, x, out)  # noqa: E731
     else:
         # fixed-size all-to-all blocks: no host synchronisation in the step, so it can be graph-captured
-        w = rank_weights(E, El, rank * El, dev)
-        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T)
+        owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
+        w = rank_weights(E, mine, dev)
+        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
         run = lambda: layer.forward(S, x)  # noqa: E731
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -505,7 +528,7 @@ def run_decode(args, world, rank, dev):
             "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
             "config": {"workload": "K3-shape decode MoE step (config 2)", "tokens": Tall, "tokens_per_gpu": T,
                        "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I, "rs": RS,
-                       "parallelism": f"ep{world}",
+                       "parallelism": f"ep{world}", "expert_placement": args.ep_placement if world > 1 else None,
                        "l2": "inputs larger than L2: each step streams the touched experts' weights"},
             "roofline": {"kernel": "whole decode layer (weights of the touched experts, slowest rank)",
                          "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -547,6 +570,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode", action="store_true", help="config 2: one 64-token decode step, us/layer")
     ap.add_argument("--decode-tokens", type=int, default=64)
+    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="N > 1: experts dealt to ranks by router bias (balanced) or in contiguous blocks")
     ap.add_argument("--zipf", action="store_true",
                     help="config 3: the routing bias makes expert popularity Zipf(1.1) (N = 1 prefill)")
     args = ap.parse_args()

@@ -101,6 +101,21 @@ class GpuOps:
         return out
 
 
+# the packing kernel writes id mod E_local for each pick; handed local ids already, this modulus keeps them
+LOCAL_IDS = 1 << 30
+
+
+def balanced_owner(bias, world):
+    """An expert placement that evens the expected load: experts in decreasing router bias (the bias is what
+    makes an expert popular) dealt to the ranks in snake order, E / world each."""
+    order = torch.argsort(torch.as_tensor(bias, dtype=torch.float32).cpu(), descending=True, stable=True)
+    owner = torch.empty(order.numel(), dtype=torch.int64)
+    for i, e in enumerate(order.tolist()):
+        rnd, pos = divmod(i, world)
+        owner[e] = pos if rnd % 2 == 0 else world - 1 - pos
+    return owner
+
+
 class EPMoELayer:
     """One rank's part of an expert-parallel MoE layer.
 
@@ -108,10 +123,13 @@ class EPMoELayer:
     [rank*E_local, (rank+1)*E_local)) and, with `shared`, the shared expert as local expert E_local.
     """
 
-    def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None, fixed_tokens=None):
+    def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None, fixed_tokens=None,
+                 owner=None):
         """fixed_tokens: when set (at most that many tokens a call), every rank sends fixed-size blocks of
         fixed_tokens*K slots to every rank, empty slots marked by local expert id -1: no host
-        synchronisation, so a whole step can be captured in a CUDA graph (decode-sized batches)."""
+        synchronisation, so a whole step can be captured in a CUDA graph (decode-sized batches).
+        owner: int [E], the rank holding each expert (E / world each; a rank's experts in increasing id order
+        are its local experts 0, 1, ...; `w` holds them in that order).  None: contiguous blocks."""
         self.fixed_tokens = fixed_tokens
         self.group = group
         self.rank = dist.get_rank(group)
@@ -121,8 +139,28 @@ class EPMoELayer:
         self.H, self.I, self.E, self.K, self.shared = H, I, E, K, int(shared)
         self.E_local = E // self.world
         self.w, self.bias, self.rs = w, bias, rs
+        self.owner_map = None
+        if owner is not None:
+            owner = torch.as_tensor(owner, dtype=torch.int64).cpu()
+            if owner.numel() != E or torch.bincount(owner, minlength=self.world).tolist() != [self.E_local] * self.world:
+                raise ValueError(f"owner must give each of {self.world} ranks {self.E_local} experts")
+            local = torch.empty(E, dtype=torch.int64)
+            for r in range(self.world):
+                mine = (owner == r).nonzero().flatten()
+                local[mine] = torch.arange(mine.numel())
+            dev = bias.device
+            self.owner_map = (owner.to(torch.int32).to(dev), local.to(torch.int32).to(dev))
         self.ops = ops or GpuOps(device)
         self.timing = None  # (dispatch_ms, combine_ms) of the last forward when events are given
+
+    def _route(self, idx):
+        """(destination rank, local expert id at the destination) of every pick, int32 [T, K] each."""
+        if self.owner_map is None:
+            dest = torch.div(idx, self.E_local, rounding_mode="floor").to(torch.int32)
+            return dest, idx - dest * self.E_local
+        owner, local = self.owner_map
+        flat = idx.reshape(-1).to(torch.int64)
+        return owner[flat].reshape(idx.shape), local[flat].reshape(idx.shape)
 
     def _a2a(self, out, inp, out_rows, in_rows):
         """All-to-all of whole rows as bytes (every backend moves uint8); splits in rows."""
@@ -140,7 +178,7 @@ class EPMoELayer:
             raise ValueError(f"{T} tokens exceed fixed_tokens={self.fixed_tokens}")
         cap = self.fixed_tokens * K
         idx, wts = ops.topk(S, self.bias, self.rs, K)
-        dest = torch.div(idx, El, rounding_mode="floor").to(torch.int32)
+        dest, lid = self._route(idx)
         plan = ops.tables(dest.reshape(-1, 1).contiguous(), W, 1)
         counts = plan.counts[:W]
         first = (torch.cumsum(counts, 0, dtype=torch.int32) - counts).to(torch.int64)
@@ -152,7 +190,7 @@ class EPMoELayer:
         send = torch.empty((n_slots, stride), dtype=torch.uint8, device=x.device)
         eid_col = H + H // 32
         send[:, eid_col:eid_col + 4].view(torch.int32).fill_(-1)  # empty slots: no expert
-        ops.pack(x, idx, slot, El, n_slots, out=send)
+        ops.pack(x, lid.contiguous(), slot, LOCAL_IDS, n_slots, out=send)
         R = n_slots + (T if self.shared else 0)
         recv = torch.empty((R, stride), dtype=torch.uint8, device=x.device)
         dist.all_to_all_single(recv[:n_slots].reshape(-1), send.reshape(-1), group=self.group)
@@ -176,12 +214,13 @@ class EPMoELayer:
         ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
         T = x.shape[0]
         idx, wts = ops.topk(S, self.bias, self.rs, K)
+        dest, lid = self._route(idx)
         # one pick a "row": several picks of a token may go to the same rank, and the table builder
         # ranks rows, so the plan runs over the expanded (token, k) sequence
-        plan = ops.tables((idx // El).to(torch.int32).reshape(-1, 1).contiguous(), W, 1)
+        plan = ops.tables(dest.reshape(-1, 1).contiguous(), W, 1)
         send_pos = plan.exp2perm.reshape(T, K)          # [T, K] slot of each pick
         send_counts = plan.counts[:W].to(torch.int64)   # picks to each rank
-        send = ops.pack(x, idx, send_pos, El, T * K)
+        send = ops.pack(x, lid.contiguous(), send_pos, LOCAL_IDS, T * K)
         recv_counts = torch.empty_like(send_counts)
         self._a2a(recv_counts, send_counts, [1] * W, [1] * W)
         sc = send_counts.tolist()
@@ -212,17 +251,20 @@ class EPMoELayer:
         return ops.combine(back, send_pos, wts, shared_rows, T, K, H)
 
 
-def slice_weights(w13, w13_sf, w2, w2_sf, E, shared, rank, world, H, I):
+def slice_weights(w13, w13_sf, w2, w2_sf, E, shared, rank, world, H, I, owner=None):
     """This rank's experts (and the shared expert, stored last) out of full tile-major weight tensors
-    laid out as k3moe_layer_forward expects (experts back to back, the shared expert after the routed)."""
+    laid out as k3moe_layer_forward expects (experts back to back, the shared expert after the routed):
+    experts [rank E/world, (rank+1) E/world), or with `owner` the experts it gives this rank, in id order."""
     El = E // world
-    e0, e1 = rank * El, (rank + 1) * El
+    mine = (list(range(rank * El, (rank + 1) * El)) if owner is None else
+            (torch.as_tensor(owner) == rank).nonzero().flatten().tolist())
 
-    def rows(t):  # the contiguous bytes of experts [e0, e1), then the shared expert's
+    def rows(t):  # the bytes of this rank's experts, then the shared expert's
         per_b = t.numel() // (E + shared)
-        parts = [t.reshape(-1)[e0 * per_b:e1 * per_b]]
+        flat = t.reshape(-1)
+        parts = [flat[e * per_b:(e + 1) * per_b] for e in mine]
         if shared:
-            parts.append(t.reshape(-1)[E * per_b:(E + 1) * per_b])
+            parts.append(flat[E * per_b:(E + 1) * per_b])
         return torch.cat(parts)
 
     return {"w13": rows(w13), "w13_sf": rows(w13_sf), "w2": rows(w2), "w2_sf": rows(w2_sf)}

@@ -24,7 +24,7 @@ def _free_port():
 CFG = dict(T=96, H=256, I=256, E=8, K=2, shared=1, rs=2.5, seed=11)
 
 
-def _worker(rank, world, port, outdir, fixed):
+def _worker(rank, world, port, outdir, mode):
     import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
@@ -43,23 +43,26 @@ def _worker(rank, world, port, outdir, fixed):
     T_l = c.T // world
     rows = slice(rank * T_l, (rank + 1) * T_l)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
-    w = k3moe_ep.slice_weights(t(c.w13), t(c.w13_sf), t(c.w2), t(c.w2_sf), c.E, c.shared, rank, world, c.H, c.I)
+    owner = k3moe_ep.balanced_owner(c.bias, world) if mode == "placed" else None
+    w = k3moe_ep.slice_weights(t(c.w13), t(c.w13_sf), t(c.w2), t(c.w2_sf), c.E, c.shared, rank, world, c.H, c.I,
+                               owner=owner)
     rs = t(np.array([c.rs_bits], np.uint16)).view(torch.bfloat16)
     layer = k3moe_ep.EPMoELayer(c.H, c.I, c.E, c.K, c.shared, w, t(c.bias), rs, ops=ep_oracle_ops.OracleOps(),
-                                fixed_tokens=T_l if fixed else None)
+                                fixed_tokens=T_l if mode == "fixed" else None, owner=owner)
     out = layer.forward(t(c.S[rows]), t(c.x_bits[rows]).view(torch.bfloat16))
     np.save(os.path.join(outdir, f"out{rank}.npy"), out.view(torch.int16).numpy().view(np.uint16))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fixed", [False, True])
-def test_ep2_gloo_matches_single_device(fixed):
-    # fixed: the fixed-block all-to-all (no counts exchange, empty slots marked -1) of decode-sized batches
+@pytest.mark.parametrize("mode", ["counts", "fixed", "placed"])
+def test_ep2_gloo_matches_single_device(mode):
+    # fixed: the fixed-block all-to-all (no counts exchange, empty slots marked -1) of decode-sized batches;
+    # placed: experts dealt to the ranks by router bias (balanced_owner) instead of in contiguous blocks
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, fixed)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, mode)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:

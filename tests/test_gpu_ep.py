@@ -1,8 +1,9 @@
 """Expert parallelism on 2 GPUs over NCCL: every rank holds half the experts
 and its own tokens; the layer's output must equal, bit for bit, the single-GPU
-layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs.  Three
-modes: the counts-exchange all-to-all, the fixed-block all-to-all, and the
-fixed-block step captured in a CUDA graph (NCCL calls inside) and replayed."""
+layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs.  Four
+modes: the counts-exchange all-to-all, the fixed-block all-to-all, the
+fixed-block step captured in a CUDA graph (NCCL calls inside) and replayed,
+and experts dealt to the ranks by router bias instead of contiguous blocks."""
 import multiprocessing as mp
 import os
 import socket
@@ -57,9 +58,10 @@ def _worker(rank, world, port, outdir, mode):
     bias = torch.from_numpy(rng.uniform(-0.1, 0.1, E).astype(np.float32)).to(dev)
     rs = torch.tensor([c["rs"]], dtype=torch.bfloat16, device=dev)
     rows = slice(rank * c["T_local"], (rank + 1) * c["T_local"])
-    w = k3moe_ep.slice_weights(w13, w13_sf, w2, w2_sf, E, sh, rank, world, H, I)
+    owner = k3moe_ep.balanced_owner(bias, world) if mode == "placed" else None
+    w = k3moe_ep.slice_weights(w13, w13_sf, w2, w2_sf, E, sh, rank, world, H, I, owner=owner)
     layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev,
-                                fixed_tokens=c["T_local"] if mode != "counts" else None)
+                                fixed_tokens=c["T_local"] if mode in ("fixed", "graph") else None, owner=owner)
     xs, Ss = x[rows].contiguous(), S[rows].contiguous()
     graph = None
     if mode == "graph":
@@ -101,7 +103,7 @@ def _worker(rank, world, port, outdir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "fixed", "graph"])
+@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed"])
 def test_ep2_nccl_bit_identical_to_one_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
