@@ -60,6 +60,15 @@ def cu_seqlens(T, n=16, seed=0):
     return np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
 
 
+def prefill_config(T, E, zipf):
+    """The `config` of the 1-GPU prefill line, the same for the GPU arm and the reference arm."""
+    return {"workload": ("K3-shape prefill MoE layer, Zipf(1.1) expert popularity (config 3)" if zipf else
+                         "K3-shape prefill MoE layer (config 1)"), "zipf": zipf,
+            "T": T, "H": H, "I": I, "E": E, "K": K, "shared_expert_width": I, "rs": RS, "global_batch": T,
+            "seq_len": T, "sequences": 16, "cu_seqlens": cu_seqlens(T).tolist(), "parallelism": "ep1",
+            "l2": "inputs larger than L2: 20.96 GB of expert weights streamed every step"}
+
+
 def layer_flops(T):
     return 6.0 * H * I * (T * K + SHARED * T)
 
@@ -214,8 +223,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
-        "config": {"workload": "K3-shape prefill MoE layer (config 1)", "T": T, "H": H, "I": I, "E": E, "K": K,
-                   "shared": SHARED, "rs": RS},
+        "config": prefill_config(T, E, None),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -760,13 +768,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
-            "config": {"workload": ("K3-shape prefill MoE layer, Zipf(1.1) expert popularity (config 3)" if zipf else
-                                    "K3-shape prefill MoE layer (config 1)"), "zipf": zipf,
-                       "T": T, "H": H, "I": I, "E": E, "K": K,
-                       "shared_expert_width": I, "rs": RS, "global_batch": T * world, "seq_len": T,
-                       "sequences": 16, "cu_seqlens": cu_seqlens(T).tolist(),
-                       "parallelism": f"dp{world} (experts replicated per GPU)" if world > 1 else "ep1",
-                       "l2": "inputs larger than L2: 20.96 GB of expert weights streamed every step"},
+            "config": prefill_config(T, E, zipf),
             "tflops": flops / (ms / 1e3) / 1e12,
             "pct_fp8_peak": flops / (ms / 1e3) / 1e12 / (FP8_PEAK_TFLOPS * world) * 100,
             "stage_ms": dict(zip(k3moe.MoELayer.STAGES, [round(float(v), 4) for v in stage_ms])),
