@@ -18,12 +18,14 @@
 //   kern_k3g_moe_route_init     source/k3_moe_route.cu:522    any grid, block 1024
 //   kern_k3_moe_w_shuffle       source/k3_moe_prefill.cu:242  grid ceil(experts*n*row_bytes/16/block)
 //   kern_k3_moe_sf_shuffle      source/k3_moe_prefill.cu:252  grid ceil(experts*n*kg/block)
+//   kern_k3_moe_front           source/k3_moe_front.cu:358    grid T + NSH/64 (T <= 64), block 1024, F_SMEM
+//                                                             dynamic shared bytes, PDL dependent
 #include "common.cuh"
 
 namespace k3 {
 namespace dropin {
 constexpr int TOPK = 16;
-constexpr int EXPERTS = 896;
+constexpr int N_EXPERTS = 896;
 constexpr int LATENT = 3584;
 constexpr int MAX_LOCAL = 1024;  // local experts the table entries handle (the reference's: 64)
 }  // namespace dropin
@@ -91,7 +93,7 @@ extern "C" __global__ void __launch_bounds__(128) kern_k3g_router_topk(const flo
   __shared__ int ce[4][TOPK_CAND];
   const int warp = threadIdx.x >> 5, b = blockIdx.x * 4 + warp;
   if (b >= B) return;
-  topk_warp<dropin::EXPERTS / 32>(S + (long long)b * dropin::EXPERTS, bias, dropin::EXPERTS, dropin::TOPK,
+  topk_warp<dropin::N_EXPERTS / 32>(S + (long long)b * dropin::N_EXPERTS, bias, dropin::N_EXPERTS, dropin::TOPK,
                                   __bfloat162float(rs[0]), threadIdx.x & 31, ck[warp], ce[warp],
                                   idx + (long long)b * dropin::TOPK, wts + (long long)b * dropin::TOPK);
 }
@@ -292,7 +294,7 @@ namespace dropin {
 constexpr int SHARED_W = 6144;               // the shared expert's width: gu = [gate | up], act = SiTU(gate, up)
 constexpr int MAX_ROWS = 8192;
 constexpr int CHUNK = 256, CHUNKS = MAX_ROWS / CHUNK, WORDS = MAX_ROWS / 32;
-constexpr int TABLE = EXPERTS * (1 + CHUNKS + WORDS);
+constexpr int TABLE = N_EXPERTS * (1 + CHUNKS + WORDS);
 constexpr int ARRIVE_AT = 0, ERR_AT = 1, GEN_AT = 32, TABLES_AT = 64;
 constexpr int SYNC_WORDS = TABLES_AT + 2 * TABLE + 2;
 constexpr int RT_THREADS = 512, RT_WARPS = RT_THREADS / 32;
@@ -312,17 +314,11 @@ __device__ __forceinline__ float tanh_approx(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
-__device__ __forceinline__ float ex2_approx_ftz(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-
 // The shared expert's activation as the reference's fused front computes it (source/k3_moe_route.cu:257-269,
-// k3_prefill_glue.cu's kern_k3g_situ): e^-g as ex2.approx.ftz(g * -log2 e), the sigmoid an IEEE reciprocal,
-// the tanh terms tanh.approx, every product and sum rounded on its own: (4 tanh(g/4) * sigmoid(g)) * 25 tanh(u/25).
+// k3_prefill_glue.cu's kern_k3g_situ): e^-g by the __expf intrinsic, the sigmoid an IEEE reciprocal, the tanh
+// terms tanh.approx, every product and sum rounded on its own: (4 tanh(g/4) * sigmoid(g)) * 25 tanh(u/25).
 __device__ __forceinline__ float situ_front(float g, float u) {
-  const float d = __fadd_rn(ex2_approx_ftz(__fmul_rn(g, -1.44269502f)), 1.0f);
+  const float d = __fadd_rn(__expf(-g), 1.0f);
   const float a = __fmul_rn(tanh_approx(__fmul_rn(g, 0.25f)), 4.0f);
   const float c = __fmul_rn(tanh_approx(__fmul_rn(u, 0.04f)), 25.0f);
   return __fmul_rn(__fmul_rn(a, __frcp_rn(d)), c);
@@ -339,7 +335,7 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
     int* __restrict__ exp2perm, int tile, int B) {
   using namespace k3::dropin;
   __shared__ u32 s_gen, s_ok;
-  __shared__ int s_cnt[EXPERTS], s_off[EXPERTS];
+  __shared__ int s_cnt[N_EXPERTS], s_off[N_EXPERTS];
   __shared__ int s_wsum[RT_WARPS];
   __shared__ u32 s_ck[RT_WARPS][TOPK_CAND];
   __shared__ int s_ce[RT_WARPS][TOPK_CAND];
@@ -354,14 +350,14 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
   u32* cur = sync + TABLES_AT + (gen & 1u) * TABLE;
   u32* nxt = sync + TABLES_AT + (~gen & 1u) * TABLE;
   int* tot = reinterpret_cast<int*>(cur);
-  int* chunk = tot + EXPERTS;
-  u32* bits = cur + EXPERTS * (1 + CHUNKS);
+  int* chunk = tot + N_EXPERTS;
+  u32* bits = cur + N_EXPERTS * (1 + CHUNKS);
   for (int i = gt; i < TABLE; i += nthreads) nxt[i] = 0u;  // the next call's table
 
   // ---- phase 1a: a warp a row: top-16, marked in this call's table
   const float rsv = __bfloat162float(rs[0]);
   for (int b = gwarp; b < B; b += nwarps) {
-    const int e = topk_warp<EXPERTS / 32>(S + (long long)b * EXPERTS, bias, EXPERTS, TOPK, rsv, lane, s_ck[warp],
+    const int e = topk_warp<N_EXPERTS / 32>(S + (long long)b * N_EXPERTS, bias, N_EXPERTS, TOPK, rsv, lane, s_ck[warp],
                                           s_ce[warp], idx + (long long)b * TOPK, wts + (long long)b * TOPK);
     if (lane < TOPK) {
       atomicAdd(tot + e, 1);
@@ -423,7 +419,7 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
 
   // ---- phase 2: CTA counts of the experts exclusive-scanned (thread t: experts 2t and 2t + 1)
   int c0 = 0, c1 = 0;
-  if (2 * t < EXPERTS) {
+  if (2 * t < N_EXPERTS) {
     s_cnt[2 * t] = __ldcg(tot + 2 * t);
     s_cnt[2 * t + 1] = __ldcg(tot + 2 * t + 1);
     c0 = (s_cnt[2 * t] + tile - 1) / tile;
@@ -442,7 +438,7 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
     before += w < warp ? s_wsum[w] : 0;
     total += s_wsum[w];
   }
-  if (2 * t < EXPERTS) {
+  if (2 * t < N_EXPERTS) {
     s_off[2 * t] = before + incl - c0 - c1;
     s_off[2 * t + 1] = before + incl - c1;
   }
@@ -451,7 +447,7 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
     num_non_exiting[0] = total;
     total_padded[0] = total * tile;
   }
-  for (int e = gt; e < EXPERTS; e += nthreads) {
+  for (int e = gt; e < N_EXPERTS; e += nthreads) {
     const int n = (s_cnt[e] + tile - 1) / tile, o = s_off[e];
     for (int c = 0; c < n; ++c) {
       cta_batch[o + c] = e;
@@ -523,4 +519,424 @@ extern "C" __global__ void kern_k3_moe_sf_shuffle(const uint8_t* __restrict__ sr
   const int c = (int)(i - row * kg);
   const int e = (int)(row / n), r = (int)(row - (long long)e * n);
   dst[(long long)e * n * kg + sf_tiled_offset(r, c, kg / 4)] = src[((long long)e * n + gemm_row_source(r, n, gated)) * kg + c];
+}
+
+// ------------------------------------------------------------------ the decode front (one launch)
+// kern_k3_moe_front (source/k3_moe_front.cu:358-471; op scripts/gen_stage.py:416-428, 1080-1087): a decode
+// step's MoE front over T <= 64 rows of the front GEMM's f32 output (F_LDS columns a row: router | latent |
+// this rank's shared gate | up).  Grid T + NSH/64 blocks of 1024 threads, F_SMEM bytes of dynamic shared
+// memory, launched as a programmatic dependent of the front GEMM (it waits at entry, then releases FC1).
+//   row block b < T   top-16 of the router columns (idx, wts: kern_k3g_router_topk's picks and bits); the
+//                     latent landed to bf16 and quantised to MXFP8 with linear scales (q, sf:
+//                     kern_k3_moe_quant's bytes); the shared expert's SiTU row (act); a flag to every
+//                     shared-expert block once the act row is in (ready), and the row's two lowest local
+//                     picks to their prefetchers (ids); the last row block to arrive (done) builds the
+//                     routing tables of this rank's experts first + j * STRIDE (j < EXPERTS / STRIDE), TILE
+//                     rows a CTA, an expert's rows in token order (the reference leaves them in atomic order;
+//                     the GEMMs compute each row on its own), padding rows routing token 0, exp2perm -1 for
+//                     another rank's expert.
+//   block T + c       sh_out[:, 64c, 64c + 64) = act . Wsh[64c, 64c + 64)^T on the tensor cores: bf16
+//                     operands, one f32 accumulation chain over K in 16-element steps in order (the order
+//                     cuBLASLt sums this shape in), rounded to bf16; its last warp pulls a share of the
+//                     first two touched experts' FC1 weights and scales into L2 while HBM is idle.
+// Carries (the manifest zeroes them once): ready / ids [NSH/64][64] i32 (each consumer clears what it read),
+// done i32 (the last row block resets the count).  Every wait is bounded (2 s); one that runs out sets bit 30
+// of done (kept until the host clears it; the count is the low 16 bits) and its block skips the work that
+// needed it instead of spinning.  The row blocks never wait and have the lower indices, so they are
+// dispatched first.  The compile-time shape takes the reference module's defines (EXPERTS, LDS, SH, STRIDE,
+// NSH) when given; the defaults are its own.
+#ifdef EXPERTS
+#define K3F_EXPERTS (EXPERTS)
+#else
+#define K3F_EXPERTS 896
+#endif
+#ifdef LDS
+#define K3F_LDS (LDS)
+#else
+#define K3F_LDS 6016
+#endif
+#ifdef SH
+#define K3F_SH (SH)
+#else
+#define K3F_SH 768
+#endif
+#ifdef STRIDE
+#define K3F_STRIDE (STRIDE)
+#else
+#define K3F_STRIDE 8
+#endif
+#ifdef NSH
+#define K3F_NSH (NSH)
+#else
+#define K3F_NSH 7168
+#endif
+
+namespace k3 {
+namespace dropin {
+constexpr int F_EXPERTS = K3F_EXPERTS, F_LDS = K3F_LDS, F_SH = K3F_SH, F_STRIDE = K3F_STRIDE, F_NSH = K3F_NSH;
+constexpr int F_LOCAL = F_EXPERTS / F_STRIDE;  // this rank's experts
+constexpr int F_TILE = 16, F_MAX_ROWS = 64;
+constexpr int F_READERS = F_NSH / 64;           // shared-expert blocks
+constexpr int F_THREADS = 1024, F_WORKERS = F_THREADS - 32;
+constexpr int F_QUANT_W0 = 1, F_QUANT_WARPS = LATENT / 8 / 32;
+constexpr int F_SITU_W0 = F_QUANT_W0 + F_QUANT_WARPS, F_SITU_THREADS = F_SH / 4;
+constexpr int F_ATOM_COL = 64 * 128;            // 64 rows of 128-byte swizzle atoms
+constexpr int F_OPERAND = F_SH / 64 * F_ATOM_COL;
+constexpr int F_SMEM = 1024 + 2 * F_OPERAND + 64 * 64 * 2;
+constexpr int F_EPI_WARPS = F_WORKERS / 128 * 4;  // warps moving accumulator tiles out (whole lane quarters)
+constexpr long long F_FC1_W = 2LL * 3072 * (LATENT / 2), F_FC1_SF = 2LL * 3072 * (LATENT / 32);
+constexpr int F_ERR = 1 << 30, F_COUNT = 0xffff;
+constexpr u64 F_WAIT_NS = 2000000000ull;
+static_assert(F_EXPERTS % 32 == 0 && F_EXPERTS / 32 <= TOPK_MAX_EPL && F_EXPERTS % F_STRIDE == 0, "router shape");
+static_assert(F_LOCAL <= F_THREADS && F_MAX_ROWS * TOPK <= F_THREADS, "one expert / one pick a thread");
+static_assert(F_SITU_THREADS % 32 == 0 && F_SITU_W0 + F_SITU_THREADS / 32 <= 32, "whole warps for the SiTU");
+static_assert(F_SH % 64 == 0 && F_NSH % 64 == 0 && F_LDS % 4 == 0, "whole swizzle atoms, 16-byte rows");
+static_assert(F_READERS <= F_WORKERS && (F_FC1_W / F_READERS) % 16 == 0 && (F_FC1_SF / F_READERS) % 16 == 0,
+              "16-byte prefetch shares");
+}  // namespace dropin
+
+__device__ __forceinline__ u32 dynamic_smem_size() {
+  u32 r;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ int ld_acquire_i32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_relaxed_i32(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_i32(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_i32(int* p, int v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int r;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(r) : "l"(p), "r"(v) : "memory");
+  return r;
+}
+// Wait (bounded) for *flag != 0; returns the value, 0 when the limit passed first.
+template <bool ACQUIRE>
+__device__ __forceinline__ int wait_nonzero(const int* flag) {
+  int v = ACQUIRE ? ld_acquire_i32(flag) : ld_relaxed_i32(flag);
+  if (v != 0) return v;
+  const u64 t0 = globaltimer_ns();
+  while ((v = ACQUIRE ? ld_acquire_i32(flag) : ld_relaxed_i32(flag)) == 0) {
+    if (globaltimer_ns() - t0 > dropin::F_WAIT_NS) return 0;
+    __nanosleep(128);
+  }
+  return v;
+}
+
+// Byte offset of row r's 16-byte chunk k (8 bf16) in a K-major operand of 128-byte swizzle atoms, 64-row
+// atom columns 8 KB apart (the tensor core's SWIZZLE_128B pattern: chunk index XOR row mod 8).
+__device__ __forceinline__ u32 front_swizzle(int r, int k) {
+  return (u32)((k >> 3) * dropin::F_ATOM_COL + r * 128 + (((k & 7) ^ (r & 7)) << 4));
+}
+// kind::f16 instruction descriptor: f32 accumulator, bf16 A and B, both K-major, M x N
+__device__ __forceinline__ u32 idesc_bf16(int m, int n) {
+  return 1u << 4 | 1u << 7 | 1u << 10 | (u32)(n >> 3) << 17 | (u32)(m >> 4) << 24;
+}
+__device__ __forceinline__ void mma_bf16(u32 d_tmem, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 8 consecutive columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld8(u32 taddr, u32 (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void front_work_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(dropin::F_WORKERS) : "memory");
+}
+
+// The last row block's routing tables over the T x 16 picks, thread i the pick i = row * 16 + k: a pick's
+// slot within its expert is the number of earlier picks of that expert (warp counts, then ranks inside the
+// warp by __match_any_sync), so an expert's rows come in token order.  Scratch in the (otherwise unused)
+// dynamic shared memory.
+__device__ __forceinline__ void front_tables(const int* __restrict__ idx, int first, int T, int* __restrict__ scratch,
+                                             int* __restrict__ cta_batch, int* __restrict__ cta_limit,
+                                             int* __restrict__ num_non_exiting, int* __restrict__ total_padded,
+                                             int* __restrict__ route_map, int* __restrict__ exp2perm) {
+  using namespace dropin;
+  int* wcnt = scratch;                 // [32 warps][F_LOCAL]: picks of each expert a warp, then their offsets
+  int* cnt = wcnt + 32 * F_LOCAL;      // [F_LOCAL]
+  int* off = cnt + F_LOCAL;            // [F_LOCAL + 1] first CTA of each expert
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  for (int i = t; i < 32 * F_LOCAL; i += F_THREADS) wcnt[i] = 0;
+  int j = -1;
+  if (t < T * TOPK) {
+    const int d = __ldcg(idx + t) - first;
+    if (d >= 0 && d % F_STRIDE == 0 && d / F_STRIDE < F_LOCAL) j = d / F_STRIDE;
+  }
+  __syncthreads();
+  const u32 same = __match_any_sync(0xffffffffu, j);
+  const int before = __popc(same & ((1u << lane) - 1u));
+  if (j >= 0 && before == 0) wcnt[warp * F_LOCAL + j] = __popc(same);
+  __syncthreads();
+  if (t < F_LOCAL) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int v = wcnt[w * F_LOCAL + t];
+      wcnt[w * F_LOCAL + t] = run;
+      run += v;
+    }
+    cnt[t] = run;
+  }
+  __syncthreads();
+  if (warp == 0) {  // off: exclusive scan of the experts' CTA counts, 32 experts a round
+    int carry = 0;
+    for (int e0 = 0; e0 < F_LOCAL; e0 += 32) {
+      const int e = e0 + lane;
+      const int ctas = e < F_LOCAL ? (cnt[e] + F_TILE - 1) / F_TILE : 0;
+      int incl = ctas;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += y;
+      }
+      if (e < F_LOCAL) off[e] = carry + incl - ctas;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      off[F_LOCAL] = carry;
+      num_non_exiting[0] = carry;
+      total_padded[0] = carry * F_TILE;
+    }
+  }
+  __syncthreads();
+  if (t < F_LOCAL) {
+    const int o0 = off[t], o1 = off[t + 1], lim = o0 * F_TILE + cnt[t];
+    for (int c = o0; c < o1; ++c) {
+      cta_batch[c] = t;
+      cta_limit[c] = min((c + 1) * F_TILE, lim);
+    }
+    for (int r = lim; r < o1 * F_TILE; ++r) route_map[r] = 0;
+  }
+  if (t < T * TOPK) {
+    int row = -1;
+    if (j >= 0) {
+      row = off[j] * F_TILE + wcnt[warp * F_LOCAL + j] + before;
+      route_map[row] = t / TOPK;
+    }
+    exp2perm[t] = row;
+  }
+}
+
+// Warp 31 of shared-expert block c: the rows' lowest local picks (clearing their flags), then this block's
+// share of the two least touched experts' FC1 weights and scales (the reference's FC1 layout: expert e's
+// [2 x 3072, LATENT] packed MXFP4 at e * F_FC1_W) into L2.
+__device__ __forceinline__ void front_prefetch(int* __restrict__ ids, int* __restrict__ done, int T, int c,
+                                               const uint8_t* __restrict__ w13, const uint8_t* __restrict__ w13_sf) {
+  using namespace dropin;
+  const int lane = threadIdx.x & 31;
+  int a = F_LOCAL, a2 = F_LOCAL;  // this lane's two least distinct local experts
+  bool ok = true;
+  for (int r = lane; r < T; r += 32) {
+    int* flag = ids + c * 64 + r;
+    const int v = wait_nonzero<false>(flag);
+    if (v == 0) {
+      ok = false;
+      continue;
+    }
+    *flag = 0;
+    const int two[2] = {(v - 1) % 256, (v - 1) / 256};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int x = two[h];
+      if (x == a || x == a2) continue;
+      if (x < a) {
+        a2 = a;
+        a = x;
+      } else if (x < a2) {
+        a2 = x;
+      }
+    }
+  }
+  if (!__all_sync(0xffffffffu, ok)) {
+    if (lane == 0) atomicOr(done, F_ERR);
+    return;
+  }
+  const int j = __reduce_min_sync(0xffffffffu, a);
+  const int k = __reduce_min_sync(0xffffffffu, a == j ? a2 : a);
+  if (lane < 2) {
+    const int e = lane ? k : j;
+    if (e < F_LOCAL) {
+      bulk_prefetch(w13 + e * F_FC1_W + c * (F_FC1_W / F_READERS), (u32)(F_FC1_W / F_READERS));
+      bulk_prefetch(w13_sf + e * F_FC1_SF + c * (F_FC1_SF / F_READERS), (u32)(F_FC1_SF / F_READERS));
+    }
+  }
+}
+
+}  // namespace k3
+
+extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_front(
+    const float* __restrict__ S, const float* __restrict__ bias, const bf16* __restrict__ rs, int* __restrict__ idx,
+    float* __restrict__ wts, uint8_t* __restrict__ q, uint8_t* __restrict__ sf, bf16* __restrict__ act,
+    int* __restrict__ ready, int* __restrict__ ids, int* __restrict__ done, int* __restrict__ cta_batch,
+    int* __restrict__ cta_limit, int* __restrict__ num_non_exiting, int* __restrict__ total_padded,
+    int* __restrict__ route_map, int* __restrict__ exp2perm, const bf16* __restrict__ wsh, bf16* __restrict__ sh_out,
+    const uint8_t* __restrict__ w13, const uint8_t* __restrict__ w13_sf, int first, int T) {
+  using namespace k3::dropin;
+  extern __shared__ uint8_t f_dyn[];
+  __shared__ u32 s_ck[TOPK_CAND];
+  __shared__ int s_ce[TOPK_CAND];
+  __shared__ int s_jmin, s_last, s_fail;
+  __shared__ u32 s_tmem;
+  __shared__ __align__(8) u64 s_bar;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  if (T < 1 || T > F_MAX_ROWS || dynamic_smem_size() < (u32)F_SMEM) {  // a launch outside the contract
+    if (b == 0 && t == 0) atomicOr(done, F_ERR);
+    return;
+  }
+
+  if (b < T) {
+    // ---------------------------------------------------------------- row block b
+    const float* row = S + (long long)b * F_LDS;
+    if (warp == 0) {
+      const int pick = topk_warp<F_EXPERTS / 32>(row, bias, F_EXPERTS, TOPK, __bfloat162float(rs[0]), lane, s_ck, s_ce,
+                                                 idx + (long long)b * TOPK, wts + (long long)b * TOPK);
+      const int d = pick - first;
+      const int mine = lane < TOPK && d >= 0 && d % F_STRIDE == 0 ? d / F_STRIDE : F_LOCAL;
+      const int j = __reduce_min_sync(0xffffffffu, mine);
+      const int j2 = __reduce_min_sync(0xffffffffu, mine == j ? F_LOCAL : mine);
+      if (lane == 0) s_jmin = j + 256 * j2;
+    } else if (warp < F_SITU_W0) {
+      // the latent: 8 columns a thread (four threads a 32-column group), landed to bf16, then MXFP8
+      const int u = t - F_QUANT_W0 * 32;
+      const float4 lo = reinterpret_cast<const float4*>(row + F_EXPERTS)[2 * u];
+      const float4 hi = reinterpret_cast<const float4*>(row + F_EXPERTS)[2 * u + 1];
+      const uint4 v = make_uint4(f2_to_bf16x2(lo.x, lo.y), f2_to_bf16x2(lo.z, lo.w), f2_to_bf16x2(hi.x, hi.y),
+                                 f2_to_bf16x2(hi.z, hi.w));
+      int sfb;
+      const uint2 w = quant8_lanes(v, sfb);
+      reinterpret_cast<uint2*>(q + (long long)b * LATENT)[u] = w;
+      if ((u & 3) == 0) sf[(long long)b * (LATENT / 32) + (u >> 2)] = (uint8_t)sfb;
+    } else if (warp < F_SITU_W0 + F_SITU_THREADS / 32) {
+      // the shared expert's SiTU, 4 columns a thread, gate and up landed to bf16 first
+      const int k = t - F_SITU_W0 * 32;
+      const float4 g = reinterpret_cast<const float4*>(row + F_EXPERTS + LATENT)[k];
+      const float4 u = reinterpret_cast<const float4*>(row + F_EXPERTS + LATENT + F_SH)[k];
+      const float2 g0 = bf16x2_to_f2(f2_to_bf16x2(g.x, g.y)), g1 = bf16x2_to_f2(f2_to_bf16x2(g.z, g.w));
+      const float2 u0 = bf16x2_to_f2(f2_to_bf16x2(u.x, u.y)), u1 = bf16x2_to_f2(f2_to_bf16x2(u.z, u.w));
+      const uint2 o = make_uint2(f2_to_bf16x2(situ_front(g0.x, u0.x), situ_front(g0.y, u0.y)),
+                                 f2_to_bf16x2(situ_front(g1.x, u1.x), situ_front(g1.y, u1.y)));
+      reinterpret_cast<uint2*>(act + (long long)b * F_SH)[k] = o;
+      // the row is in: one flag to each shared-expert block
+      asm volatile("bar.sync 2, %0;" ::"n"(F_SITU_THREADS) : "memory");
+      __threadfence();
+      for (int c = k; c < F_READERS; c += F_SITU_THREADS) st_release_i32(ready + c * 64 + b, 1);
+    }
+    __syncthreads();
+    for (int c = t; c < F_READERS; c += F_THREADS) st_relaxed_i32(ids + c * 64 + b, s_jmin + 1);
+    if (t == 0) {
+      __threadfence();
+      const int n = atom_add_acq_rel(done, 1);
+      s_last = (n & F_COUNT) == T - 1;
+      __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    front_tables(idx, first, T, reinterpret_cast<int*>(f_dyn), cta_batch, cta_limit, num_non_exiting, total_padded,
+                 route_map, exp2perm);
+    __syncthreads();
+    if (t == 0) atomicAnd(done, F_ERR);  // the count back to zero, a recorded error kept
+    return;
+  }
+
+  // ------------------------------------------------------------------ block T + c: shared down projection
+  const int c = b - T, n0 = c * 64;
+  if (warp == 31) {
+    front_prefetch(ids, done, T, c, w13, w13_sf);
+    return;
+  }
+  uint8_t* sw = f_dyn + ((1024u - (smem_u32(f_dyn) & 1023u)) & 1023u);  // Wsh rows, 1 KB aligned
+  uint8_t* sa = sw + F_OPERAND;                                       // the T act rows
+  bf16* tile = reinterpret_cast<bf16*>(sa + F_OPERAND);               // out [T][64]
+  const u32 sw_at = smem_u32(sw), sa_at = smem_u32(sa);
+  for (int i = t; i < 64 * (F_SH / 8); i += F_WORKERS) {  // the weights need no flag: in flight at once
+    const int r = i / (F_SH / 8), k = i % (F_SH / 8);
+    cp_async16(sw_at + front_swizzle(r, k), wsh + (long long)(n0 + r) * F_SH + k * 8);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, 64);
+    tmem_relinquish();
+  }
+  if (t == 0) {
+    s_fail = 0;
+    mbar_init(&s_bar, 1);
+    fence_mbar_init();
+  }
+  front_work_sync();
+  if (t < T) {
+    int* flag = ready + c * 64 + t;
+    if (wait_nonzero<true>(flag) != 0) {
+      *flag = 0;
+    } else {
+      s_fail = 1;
+      atomicOr(done, F_ERR);
+    }
+  }
+  front_work_sync();
+  const bool fail = *reinterpret_cast<volatile int*>(&s_fail) != 0;
+  if (!fail)
+    for (int i = t; i < T * (F_SH / 8); i += F_WORKERS) {
+      const int r = i / (F_SH / 8), k = i % (F_SH / 8);
+      cp_async16(sa_at + front_swizzle(r, k), act + (long long)r * F_SH + k * 8);
+    }
+  cp_async_wait_all();
+  fence_proxy_async_shared();  // the operands, to the tensor core's reads
+  tc_fence_before();
+  front_work_sync();
+  tc_fence_after();
+  const int tiles = (T + 7) / 8;
+  if (!fail) {
+    if (t == 0) {
+      const u32 idesc = idesc_bf16(64, tiles * 8);
+      for (int s = 0; s < F_SH / 16; ++s) {  // K in 16-element steps, one accumulation chain in order
+        const u32 off = (u32)((s >> 2) * F_ATOM_COL + (s & 3) * 32);
+        mma_bf16(s_tmem, sdesc_k_sw128(sw_at + off), sdesc_k_sw128(sa_at + off), idesc, s > 0 ? 1u : 0u);
+      }
+      tc_commit(&s_bar);
+    }
+    __syncwarp();
+    if (warp < F_EPI_WARPS && mbar_wait(&s_bar, 0, nullptr, nullptr, 0, F_WAIT_NS)) {
+      tc_fence_after();
+      // M = 64: accumulator row m (output column n0 + m) sits in lane 32 (m / 16) + m % 16, column = token
+      const int quarter = warp & 3;
+      for (int j = warp >> 2; j < tiles; j += F_EPI_WARPS / 4) {
+        u32 v[8];
+        tmem_ld8(s_tmem + ((u32)(32 * quarter) << 16) + 8 * j, v);
+        tmem_wait_ld();
+        if (lane < 16)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            tile[(8 * j + i) * 64 + 16 * quarter + lane] = __float2bfloat16(__uint_as_float(v[i]));
+      }
+    }
+  }
+  tc_fence_before();
+  front_work_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(s_tmem, 64);
+  }
+  if (!fail)
+    for (int i = t; i < T * 8; i += F_WORKERS) {
+      const int r = i >> 3, col = i & 7;
+      reinterpret_cast<uint4*>(sh_out + (long long)r * F_NSH + n0)[col] = reinterpret_cast<const uint4*>(tile + r * 64)[col];
+    }
 }

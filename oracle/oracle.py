@@ -200,3 +200,22 @@ def moe_forward(S, bias, rs_bits, x_bits, w13, w13_sf, w2, w2_sf, E, K, H, I, sh
     y = fc2(w2, w2_sf, f1q, f1sf, tb["cta_batch"], tb["cta_limit"], 0, nne, H, I)
     out = combine(y, tb["exp2perm"], wts, tb["meta"], T, K)
     return out, dict(idx=idx, wts=wts, tables=tb, q_perm=qp, sf_perm=sfp, fc1_q=f1q, fc1_sf=f1sf, fc2=y)
+
+
+def situ(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    """K3's shared-expert activation in float64 (harness/k3/ref.h:97-101; source/k3_moe_front.cu:76-83):
+    4 tanh(g/4) * sigmoid(g) * 25 tanh(u/25), g and u as given (land them to bf16 first where the kernel does)."""
+    g = np.asarray(g, np.float64)
+    u = np.asarray(u, np.float64)
+    return 4.0 * np.tanh(g / 4.0) / (1.0 + np.exp(-g)) * 25.0 * np.tanh(u / 25.0)
+
+
+def strided_tables(idx: np.ndarray, first: int, stride: int, local: int, tile: int = 16):
+    """Routing tables of a rank holding experts first + j * stride (j < local): the decode front's
+    (source/k3_moe_front.cu:119-176), an expert's rows in token order.  Picks of other ranks' experts get
+    exp2perm -1."""
+    idx = np.asarray(idx, np.int64)
+    d = idx - first
+    mine = (d >= 0) & (d % stride == 0) & (d // stride < local)
+    loc = np.where(mine, d // stride, -1).astype(np.int32)
+    return tables(loc, local, 0, 0, tile)

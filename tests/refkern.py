@@ -51,6 +51,15 @@ def function(module: str, entry: str):
     return f
 
 
+def allow_smem(f, nbytes: int):
+    """Let `f` launch with `nbytes` of dynamic shared memory (CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES)."""
+    d = _drv()
+    d.cuFuncSetAttribute.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+    rc = d.cuFuncSetAttribute(f, 8, int(nbytes))
+    if rc != 0:
+        raise RuntimeError(f"cuFuncSetAttribute = {rc}")
+
+
 def launch(f, grid, block, args, smem=0):
     """args: ctypes values (c_void_p for device pointers, c_int for ints)."""
     holders = [ctypes.pointer(a) for a in args]

@@ -232,3 +232,121 @@ def test_weight_shuffles(dev, experts, n, K, gated):
     total = experts * n * kg
     ro, o = _both("k3_moe_prefill", "kern_k3_moe_sf_shuffle", ((total + 255) // 256, 1, 1), (256, 1, 1), mk_sf)
     assert torch.equal(o, ro)
+
+
+FRONT_LDS, FRONT_SH, FRONT_STRIDE, FRONT_NSH = 6016, 768, 8, 7168
+FRONT_LOCAL, FRONT_READERS, FRONT_TILE = E // FRONT_STRIDE, FRONT_NSH // 64, 16
+FRONT_SMEM = 1024 + 2 * (FRONT_SH // 64) * 64 * 128 + 64 * 64 * 2
+FC1_W, FC1_SF = 2 * 3072 * (LATENT // 2), 2 * 3072 * (LATENT // 32)
+FRONT_CTAS = 256
+
+
+@pytest.fixture(scope="module")
+def front_weights(dev):
+    """The shared expert's down projection [NSH, SH] bf16 and FC1 buffers the prefetcher reads (contents unused)."""
+    rng = np.random.default_rng(77)
+    wsh = _t(oracle.bf16_bits((0.05 * rng.standard_normal((FRONT_NSH, FRONT_SH))).astype(np.float32)),
+             dev).view(torch.bfloat16)
+    w13 = torch.zeros(FRONT_LOCAL * FC1_W, dtype=torch.uint8, device=dev)
+    w13_sf = torch.zeros(FRONT_LOCAL * FC1_SF, dtype=torch.uint8, device=dev)
+    return wsh, w13, w13_sf
+
+
+def _front_inputs(T, ties, seed, dev):
+    rng = np.random.default_rng(seed)
+    if ties:  # many equal scores: the tie rule (smaller expert first) decides the picks
+        S = (rng.integers(-6, 7, (T, FRONT_LDS)) * 0.5).astype(np.float32)
+        bias = np.zeros(E, np.float32)
+    else:
+        S = rng.uniform(-4, 4, (T, FRONT_LDS)).astype(np.float32)
+        bias = rng.uniform(-0.1, 0.1, E).astype(np.float32)
+    return S, bias
+
+
+def _front_run(module, calls, weights, dev):
+    """Launch `module`'s kern_k3_moe_front once per (T, S, bias, rs_bits, first) in order, on one set of
+    carries (ready, ids, done) zeroed once before the first call, as the manifest keeps them."""
+    wsh, w13, w13_sf = weights
+    f = rk.function(module, "kern_k3_moe_front")
+    rk.allow_smem(f, FRONT_SMEM)
+    ready = torch.zeros(FRONT_READERS * 64, dtype=torch.int32, device=dev)
+    ids = torch.zeros(FRONT_READERS * 64, dtype=torch.int32, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    outs = []
+    for T, S, bias, rs_bits, first in calls:
+        S_d, bias_d = _t(S, dev), _t(bias, dev)
+        rs = _t(np.array([rs_bits], np.uint16), dev).view(torch.bfloat16)
+        o = dict(idx=_poison((T, TOPK), torch.int32, dev), wts=_poison((T, TOPK), torch.float32, dev),
+                 q=_poison((T, LATENT), torch.uint8, dev), sf=_poison((T, LATENT // 32), torch.uint8, dev),
+                 act=_poison((T, FRONT_SH), torch.bfloat16, dev),
+                 cta_batch=_poison((FRONT_CTAS,), torch.int32, dev), cta_limit=_poison((FRONT_CTAS,), torch.int32, dev),
+                 nne=_poison((1,), torch.int32, dev), tp=_poison((1,), torch.int32, dev),
+                 route_map=_poison((FRONT_CTAS * FRONT_TILE,), torch.int32, dev),
+                 exp2perm=_poison((T, TOPK), torch.int32, dev), sh_out=_poison((T, FRONT_NSH), torch.bfloat16, dev))
+        args = [rk.P(S_d), rk.P(bias_d), rk.P(rs), rk.P(o["idx"]), rk.P(o["wts"]), rk.P(o["q"]), rk.P(o["sf"]),
+                rk.P(o["act"]), rk.P(ready), rk.P(ids), rk.P(done), rk.P(o["cta_batch"]), rk.P(o["cta_limit"]),
+                rk.P(o["nne"]), rk.P(o["tp"]), rk.P(o["route_map"]), rk.P(o["exp2perm"]), rk.P(wsh),
+                rk.P(o["sh_out"]), rk.P(w13), rk.P(w13_sf), rk.I(first), rk.I(T)]
+        rk.launch(f, (T + FRONT_READERS, 1, 1), (1024, 1, 1), args, smem=FRONT_SMEM)
+        torch.cuda.synchronize()
+        o["carries"] = (int(ready.abs().sum().item()), int(ids.abs().sum().item()), int(done.item()))
+        outs.append({k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in o.items()})
+    return outs
+
+
+@pytest.mark.parametrize("ties", [0, 1])
+def test_decode_front(dev, front_weights, ties):
+    """kern_k3_moe_front over a run of calls (1-64 rows, several ranks' expert slices) on one set of carries:
+    picks, weights, the latent's MXFP8, the SiTU row and the shared expert's down projection byte-equal to
+    the reference entry's; the routing tables equal to the oracle's (an expert's rows in token order) and
+    to the reference's up to the order of an expert's rows (it places rows by shared-memory atomics);
+    every carry back to zero after each call."""
+    rs_bits = 0x4020  # 2.5
+    calls = []
+    for n, (T, first) in enumerate([(1, 0), (8, 3), (24, 7), (48, 1), (64, 0), (17, 5)]):
+        S, bias = _front_inputs(T, ties, 1000 * ties + n, dev)
+        calls.append((T, S, bias, rs_bits, first))
+    ref = _front_run("k3_moe_front", calls, front_weights, dev)
+    got = _front_run(MOD, calls, front_weights, dev)
+    wsh = front_weights[0].float().cpu()
+    for (T, S, bias, _, first), r, g in zip(calls, ref, got):
+        tag = f"T={T} first={first}"
+        assert g["carries"] == (0, 0, 0), f"{tag}: carries left set {g['carries']}"
+        assert r["carries"] == (0, 0, 0), f"{tag}: reference carries {r['carries']}"
+        for name in ("idx", "wts", "q", "sf", "act", "sh_out", "nne", "tp"):
+            assert torch.equal(r[name].view(torch.uint8), g[name].view(torch.uint8)), f"{tag}: {name} differs"
+        nne, tp = int(g["nne"][0]), int(g["tp"][0])
+        assert torch.equal(r["cta_batch"][:nne], g["cta_batch"][:nne]) and torch.equal(r["cta_limit"][:nne],
+                                                                                       g["cta_limit"][:nne])
+        # the oracle: picks, the SiTU row, token-ordered tables, the projection in f32
+        idx_o, wts_o = oracle.topk(S[:, :E], bias, rs_bits, TOPK)
+        assert np.array_equal(g["idx"].numpy(), idx_o), tag
+        # the host's expf and the device's differ by an ulp now and then: weights to 2e-6 (bit-equal to the
+        # reference entry above)
+        np.testing.assert_allclose(g["wts"].numpy(), wts_o, rtol=2e-6, atol=0, err_msg=tag)
+        q_o, sf_o = oracle.quant_mxfp8(oracle.bf16_bits(S[:, E:E + LATENT]))
+        assert np.array_equal(g["q"].numpy(), q_o) and np.array_equal(g["sf"].numpy(), sf_o), tag
+        land = lambda a: oracle.bf16_to_f32(oracle.bf16_bits(a))  # noqa: E731
+        gate, up = S[:, E + LATENT:E + LATENT + FRONT_SH], S[:, E + LATENT + FRONT_SH:E + LATENT + 2 * FRONT_SH]
+        act_o = oracle.situ(land(gate), land(up))
+        act_g = g["act"].float().numpy()
+        assert np.allclose(act_g, act_o, rtol=1.6e-2, atol=1e-3), f"{tag}: SiTU off the oracle"
+        tb = oracle.strided_tables(idx_o, first, FRONT_STRIDE, FRONT_LOCAL, FRONT_TILE)
+        assert nne == tb["meta"][0] and tp == tb["meta"][1], tag
+        assert np.array_equal(g["cta_batch"][:nne].numpy(), tb["cta_batch"][:nne]), tag
+        assert np.array_equal(g["cta_limit"][:nne].numpy(), tb["cta_limit"][:nne]), tag
+        assert np.array_equal(g["route_map"][:tp].numpy(), tb["route_map"][:tp]), tag
+        assert np.array_equal(g["exp2perm"].numpy(), tb["exp2perm"]), tag
+        # the reference's tables: the same rows per expert in another order
+        e2r, rmr, cb = r["exp2perm"].numpy().ravel(), r["route_map"].numpy(), r["cta_batch"].numpy()
+        e2g = g["exp2perm"].numpy().ravel()
+        for i in range(T * TOPK):
+            assert (e2r[i] < 0) == (e2g[i] < 0), f"{tag}: pick {i}"
+            if e2r[i] >= 0:
+                assert rmr[e2r[i]] == i // TOPK and cb[e2r[i] // FRONT_TILE] == cb[e2g[i] // FRONT_TILE], f"{tag}: {i}"
+        pad = np.ones(tp, bool)
+        pad[e2g[e2g >= 0]] = False
+        assert (rmr[:tp][pad] == 0).all(), f"{tag}: reference padding rows"
+        want = act_g.astype(np.float32) @ wsh.numpy().T
+        got_sh = g["sh_out"].float().numpy()
+        assert np.allclose(got_sh, want, rtol=1e-2, atol=2e-2 * np.abs(want).max()), f"{tag}: projection"
