@@ -578,8 +578,10 @@ constexpr int F_LOCAL = F_EXPERTS / F_STRIDE;  // this rank's experts
 constexpr int F_TILE = 16, F_MAX_ROWS = 64;
 constexpr int F_READERS = F_NSH / 64;           // shared-expert blocks
 constexpr int F_THREADS = 1024, F_WORKERS = F_THREADS - 32;
-constexpr int F_QUANT_W0 = 1, F_QUANT_WARPS = LATENT / 8 / 32;
-constexpr int F_SITU_W0 = F_QUANT_W0 + F_QUANT_WARPS, F_SITU_THREADS = F_SH / 4;
+constexpr int F_SORT_WARPS = F_EXPERTS / 32;    // an expert a thread
+constexpr int F_QUANT_WARPS = LATENT / 8 / 32;  // 8 latent columns a thread
+constexpr int F_RANK_WARPS = F_SORT_WARPS - F_QUANT_WARPS;
+constexpr int F_SITU_THREADS = F_SH / 4;        // 4 shared columns a thread
 constexpr int F_ATOM_COL = 64 * 128;            // 64 rows of 128-byte swizzle atoms
 constexpr int F_OPERAND = F_SH / 64 * F_ATOM_COL;
 constexpr int F_SMEM = 1024 + 2 * F_OPERAND + 64 * 64 * 2;
@@ -589,7 +591,8 @@ constexpr int F_ERR = 1 << 30, F_COUNT = 0xffff;
 constexpr u64 F_WAIT_NS = 2000000000ull;
 static_assert(F_EXPERTS % 32 == 0 && F_EXPERTS / 32 <= TOPK_MAX_EPL && F_EXPERTS % F_STRIDE == 0, "router shape");
 static_assert(F_LOCAL <= F_THREADS && F_MAX_ROWS * TOPK <= F_THREADS, "one expert / one pick a thread");
-static_assert(F_SITU_THREADS % 32 == 0 && F_SITU_W0 + F_SITU_THREADS / 32 <= 32, "whole warps for the SiTU");
+static_assert(F_RANK_WARPS >= 1 && F_SORT_WARPS <= 31 && F_SORT_WARPS >= TOPK,
+              "ranking warps, a warp left for the SiTU, at least TOPK warp maxima");
 static_assert(F_SH % 64 == 0 && F_NSH % 64 == 0 && F_LDS % 4 == 0, "whole swizzle atoms, 16-byte rows");
 static_assert(F_READERS <= F_WORKERS && (F_FC1_W / F_READERS) % 16 == 0 && (F_FC1_SF / F_READERS) % 16 == 0,
               "16-byte prefetch shares");
@@ -685,14 +688,16 @@ __device__ __forceinline__ void front_tables(const int* __restrict__ idx, int fi
   const int before = __popc(same & ((1u << lane) - 1u));
   if (j >= 0 && before == 0) wcnt[warp * F_LOCAL + j] = __popc(same);
   __syncthreads();
-  if (t < F_LOCAL) {
-    int run = 0;
-    for (int w = 0; w < 32; ++w) {
-      const int v = wcnt[w * F_LOCAL + t];
-      wcnt[w * F_LOCAL + t] = run;
-      run += v;
+  for (int e = warp; e < F_LOCAL; e += 32) {  // an expert a warp, lane w holding warp w's count
+    const int v = wcnt[lane * F_LOCAL + e];
+    int incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
     }
-    cnt[t] = run;
+    wcnt[lane * F_LOCAL + e] = incl - v;
+    if (lane == 31) cnt[e] = incl;
   }
   __syncthreads();
   if (warp == 0) {  // off: exclusive scan of the experts' CTA counts, 32 experts a round
@@ -790,9 +795,7 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
     const uint8_t* __restrict__ w13, const uint8_t* __restrict__ w13_sf, int first, int T) {
   using namespace k3::dropin;
   extern __shared__ uint8_t f_dyn[];
-  __shared__ u32 s_ck[TOPK_CAND];
-  __shared__ int s_ce[TOPK_CAND];
-  __shared__ int s_jmin, s_last, s_fail;
+  __shared__ int s_last, s_fail;
   __shared__ u32 s_tmem;
   __shared__ __align__(8) u64 s_bar;
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -805,52 +808,130 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
 
   if (b < T) {
     // ---------------------------------------------------------------- row block b
+    // Warps [0, F_SORT_WARPS) hold one expert a thread: sigmoid, key, the warp maxima; tau (the 16th largest
+    // warp maximum, computed by every warp alike) bounds the top 16 from below, so only keys >= tau are
+    // candidates; they are compacted into shared memory and ranked in parallel (a warp a candidate, its
+    // lanes counting the candidates ahead of it), the ranks < 16 giving the picks in order.  The latent's
+    // MXFP8 runs on warps [F_RANK_WARPS, F_SORT_WARPS) meanwhile, the SiTU on the remaining warps from the
+    // start.
     const float* row = S + (long long)b * F_LDS;
-    if (warp == 0) {
-      const int pick = topk_warp<F_EXPERTS / 32>(row, bias, F_EXPERTS, TOPK, __bfloat162float(rs[0]), lane, s_ck, s_ce,
-                                                 idx + (long long)b * TOPK, wts + (long long)b * TOPK);
-      const int d = pick - first;
-      const int mine = lane < TOPK && d >= 0 && d % F_STRIDE == 0 ? d / F_STRIDE : F_LOCAL;
-      const int j = __reduce_min_sync(0xffffffffu, mine);
-      const int j2 = __reduce_min_sync(0xffffffffu, mine == j ? F_LOCAL : mine);
-      if (lane == 0) s_jmin = j + 256 * j2;
-    } else if (warp < F_SITU_W0) {
-      // the latent: 8 columns a thread (four threads a 32-column group), landed to bf16, then MXFP8
-      const int u = t - F_QUANT_W0 * 32;
-      const float4 lo = reinterpret_cast<const float4*>(row + F_EXPERTS)[2 * u];
-      const float4 hi = reinterpret_cast<const float4*>(row + F_EXPERTS)[2 * u + 1];
-      const uint4 v = make_uint4(f2_to_bf16x2(lo.x, lo.y), f2_to_bf16x2(lo.z, lo.w), f2_to_bf16x2(hi.x, hi.y),
-                                 f2_to_bf16x2(hi.z, hi.w));
-      int sfb;
-      const uint2 w = quant8_lanes(v, sfb);
-      reinterpret_cast<uint2*>(q + (long long)b * LATENT)[u] = w;
-      if ((u & 3) == 0) sf[(long long)b * (LATENT / 32) + (u >> 2)] = (uint8_t)sfb;
-    } else if (warp < F_SITU_W0 + F_SITU_THREADS / 32) {
-      // the shared expert's SiTU, 4 columns a thread, gate and up landed to bf16 first
-      const int k = t - F_SITU_W0 * 32;
-      const float4 g = reinterpret_cast<const float4*>(row + F_EXPERTS + LATENT)[k];
-      const float4 u = reinterpret_cast<const float4*>(row + F_EXPERTS + LATENT + F_SH)[k];
-      const float2 g0 = bf16x2_to_f2(f2_to_bf16x2(g.x, g.y)), g1 = bf16x2_to_f2(f2_to_bf16x2(g.z, g.w));
-      const float2 u0 = bf16x2_to_f2(f2_to_bf16x2(u.x, u.y)), u1 = bf16x2_to_f2(f2_to_bf16x2(u.z, u.w));
-      const uint2 o = make_uint2(f2_to_bf16x2(situ_front(g0.x, u0.x), situ_front(g0.y, u0.y)),
-                                 f2_to_bf16x2(situ_front(g1.x, u1.x), situ_front(g1.y, u1.y)));
-      reinterpret_cast<uint2*>(act + (long long)b * F_SH)[k] = o;
-      // the row is in: one flag to each shared-expert block
-      asm volatile("bar.sync 2, %0;" ::"n"(F_SITU_THREADS) : "memory");
-      __threadfence();
-      for (int c = k; c < F_READERS; c += F_SITU_THREADS) st_release_i32(ready + c * 64 + b, 1);
-    }
-    __syncthreads();
-    for (int c = t; c < F_READERS; c += F_THREADS) st_relaxed_i32(ids + c * 64 + b, s_jmin + 1);
-    if (t == 0) {
-      __threadfence();
-      const int n = atom_add_acq_rel(done, 1);
-      s_last = (n & F_COUNT) == T - 1;
-      __threadfence();
+    float* s_sig = reinterpret_cast<float*>(f_dyn);                 // [F_EXPERTS]
+    u32* c_key = reinterpret_cast<u32*>(s_sig + F_EXPERTS);         // candidates [F_EXPERTS]
+    int* c_e = reinterpret_cast<int*>(c_key + F_EXPERTS);           // [F_EXPERTS]
+    u32* s_wmax = reinterpret_cast<u32*>(c_e + F_EXPERTS);          // [32]
+    int* s_pick = reinterpret_cast<int*>(s_wmax + 32);              // [TOPK]
+    int* s_n = s_pick + TOPK;
+    int* table_scratch = s_n + 32;
+    if (warp < F_SORT_WARPS) {
+      // the latent's loads in flight from the start (quantised after the ranking)
+      float4 lat_lo = make_float4(0.f, 0.f, 0.f, 0.f), lat_hi = lat_lo;
+      const int u = t - F_RANK_WARPS * 32;
+      if (warp >= F_RANK_WARPS) {
+        lat_lo = reinterpret_cast<const float4*>(row + F_EXPERTS)[2 * u];
+        lat_hi = reinterpret_cast<const float4*>(row + F_EXPERTS)[2 * u + 1];
+      }
+      const float rsv = __bfloat162float(rs[0]);
+      const float sg = router_sigmoid(row[t]);
+      const u32 key = ord_f32(sg + bias[t]);
+      s_sig[t] = sg;
+      const u32 m = __reduce_max_sync(0xffffffffu, key);
+      if (lane == 0) s_wmax[warp] = m;
+      if (t == 0) *s_n = 0;
+      asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
+      u32 v = lane < F_SORT_WARPS ? s_wmax[lane] : 0u;
+#pragma unroll
+      for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          const u32 p = __shfl_xor_sync(0xffffffffu, v, j);
+          v = (((lane & k) == 0) == ((lane & j) == 0)) ? max(v, p) : min(v, p);  // descending
+        }
+      const u32 tau = __shfl_sync(0xffffffffu, v, TOPK - 1);
+      const bool cand = key >= tau;
+      const u32 bal = __ballot_sync(0xffffffffu, cand);
+      int at = 0;
+      if (lane == 0) at = atomicAdd(s_n, __popc(bal));
+      at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & ((1u << lane) - 1u));
+      if (cand) {
+        c_key[at] = key;
+        c_e[at] = t;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
+      if (warp < F_RANK_WARPS) {
+        // candidate i's rank: the candidates with a larger key, or the same key and a smaller expert
+        const int n = *s_n;
+        for (int i = warp; i < n; i += F_RANK_WARPS) {
+          const u32 ki = c_key[i];
+          const int ei = c_e[i];
+          int ahead = 0;
+          for (int qq = lane; qq < n; qq += 32) {
+            const u32 kq = c_key[qq];
+            ahead += (kq > ki) | ((kq == ki) & (c_e[qq] < ei));
+          }
+          ahead = __reduce_add_sync(0xffffffffu, ahead);
+          if (lane == 0 && ahead < TOPK) s_pick[ahead] = ei;
+        }
+      } else {
+        // the latent: 8 columns a thread (four threads a 32-column group), landed to bf16, then MXFP8
+        const uint4 lv = make_uint4(f2_to_bf16x2(lat_lo.x, lat_lo.y), f2_to_bf16x2(lat_lo.z, lat_lo.w),
+                                    f2_to_bf16x2(lat_hi.x, lat_hi.y), f2_to_bf16x2(lat_hi.z, lat_hi.w));
+        int sfb;
+        const uint2 w = quant8_lanes(lv, sfb);
+        reinterpret_cast<uint2*>(q + (long long)b * LATENT)[u] = w;
+        if ((u & 3) == 0) sf[(long long)b * (LATENT / 32) + (u >> 2)] = (uint8_t)sfb;
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
+      if (warp == 0) {
+        const int pick = lane < TOPK ? s_pick[lane] : 0;
+        const float w = lane < TOPK ? s_sig[pick] : 0.f;
+        float den = w;
+#pragma unroll
+        for (int off = TOPK / 2; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+        if (lane < TOPK) {
+          wts[(long long)b * TOPK + lane] = (w / (den + 1e-20f)) * rsv;
+          idx[(long long)b * TOPK + lane] = pick;
+        }
+        // the row's two lowest local picks, to every shared-expert block's prefetcher
+        const int d = pick - first;
+        const int mine = lane < TOPK && d >= 0 && d % F_STRIDE == 0 ? d / F_STRIDE : F_LOCAL;
+        const int j = __reduce_min_sync(0xffffffffu, mine);
+        const int j2 = __reduce_min_sync(0xffffffffu, mine == j ? F_LOCAL : mine);
+        for (int c = lane; c < F_READERS; c += 32) st_relaxed_i32(ids + c * 64 + b, 1 + j + 256 * j2);
+        __syncwarp();
+        if (lane == 0) {  // this row's picks are out: count the row in (release them, acquire the others')
+          const int n = atom_add_acq_rel(done, 1);
+          s_last = (n & F_COUNT) == T - 1;
+        }
+      }
+    } else {
+      // the shared expert's SiTU, 4 columns a thread, gate and up landed to bf16 first; every pass's loads
+      // in flight before the first is used
+      constexpr int LANES = F_THREADS - F_SORT_WARPS * 32, PASSES = (F_SITU_THREADS + LANES - 1) / LANES;
+      const int k0 = t - F_SORT_WARPS * 32;
+      float4 g[PASSES], u[PASSES];
+#pragma unroll
+      for (int p = 0; p < PASSES; ++p)
+        if (k0 + p * LANES < F_SITU_THREADS) {
+          g[p] = reinterpret_cast<const float4*>(row + F_EXPERTS + LATENT)[k0 + p * LANES];
+          u[p] = reinterpret_cast<const float4*>(row + F_EXPERTS + LATENT + F_SH)[k0 + p * LANES];
+        }
+#pragma unroll
+      for (int p = 0; p < PASSES; ++p)
+        if (k0 + p * LANES < F_SITU_THREADS) {
+          const float2 g0 = bf16x2_to_f2(f2_to_bf16x2(g[p].x, g[p].y)), g1 = bf16x2_to_f2(f2_to_bf16x2(g[p].z, g[p].w));
+          const float2 u0 = bf16x2_to_f2(f2_to_bf16x2(u[p].x, u[p].y)), u1 = bf16x2_to_f2(f2_to_bf16x2(u[p].z, u[p].w));
+          const uint2 o = make_uint2(f2_to_bf16x2(situ_front(g0.x, u0.x), situ_front(g0.y, u0.y)),
+                                     f2_to_bf16x2(situ_front(g1.x, u1.x), situ_front(g1.y, u1.y)));
+          reinterpret_cast<uint2*>(act + (long long)b * F_SH)[k0 + p * LANES] = o;
+        }
+      // the row is in: one flag to each shared-expert block (a release after the barrier: cumulative over
+      // the SiTU warps' stores)
+      asm volatile("bar.sync 3, %0;" ::"n"(LANES) : "memory");
+      for (int c = k0; c < F_READERS; c += LANES) st_release_i32(ready + c * 64 + b, 1);
     }
     __syncthreads();
     if (!s_last) return;
-    front_tables(idx, first, T, reinterpret_cast<int*>(f_dyn), cta_batch, cta_limit, num_non_exiting, total_padded,
+    front_tables(idx, first, T, table_scratch, cta_batch, cta_limit, num_non_exiting, total_padded,
                  route_map, exp2perm);
     __syncthreads();
     if (t == 0) atomicAnd(done, F_ERR);  // the count back to zero, a recorded error kept
