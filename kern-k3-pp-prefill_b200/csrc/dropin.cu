@@ -590,8 +590,15 @@ constexpr long long F_FC1_W = 2LL * 3072 * (LATENT / 2), F_FC1_SF = 2LL * 3072 *
 constexpr int F_ERR = 1 << 30, F_COUNT = 0xffff;
 constexpr u64 F_WAIT_NS = 2000000000ull;
 static_assert(F_EXPERTS % 32 == 0 && F_EXPERTS / 32 <= TOPK_MAX_EPL && F_EXPERTS % F_STRIDE == 0, "router shape");
-static_assert(F_LOCAL <= F_THREADS && F_MAX_ROWS * TOPK <= F_THREADS, "one expert / one pick a thread");
-static_assert(F_RANK_WARPS >= 1 && F_SORT_WARPS <= 31 && F_SORT_WARPS >= TOPK,
+static_assert(F_LOCAL <= F_THREADS - F_SORT_WARPS * 32 && F_MAX_ROWS * TOPK <= F_THREADS,
+              "an expert mask a SiTU thread to zero, one pick a thread");
+static_assert(F_MAX_ROWS <= 64, "an expert's picking rows fit a 64-bit mask");
+static_assert(F_SORT_WARPS % 4 == 0, "warp maxima read four at a time");
+
+constexpr int F_LOCAL_SITU_ROWS = 8;
+static_assert(F_LOCAL_SITU_ROWS * (F_SH / 8) <= F_WORKERS, "one act chunk a thread");  // up to this many rows every shared-expert block computes the SiTU rows
+                                       // itself instead of waiting for the row blocks' flags
+static_assert(F_RANK_WARPS >= 2 && F_SORT_WARPS <= 31 && F_SORT_WARPS >= TOPK,
               "ranking warps, a warp left for the SiTU, at least TOPK warp maxima");
 static_assert(F_SH % 64 == 0 && F_NSH % 64 == 0 && F_LDS % 4 == 0, "whole swizzle atoms, 16-byte rows");
 static_assert(F_READERS <= F_WORKERS && (F_FC1_W / F_READERS) % 16 == 0 && (F_FC1_SF / F_READERS) % 16 == 0,
@@ -637,6 +644,12 @@ __device__ __forceinline__ int wait_nonzero(const int* flag) {
   return v;
 }
 
+// Two SiTU outputs as a bf16 pair: gate and up landed to bf16 first (the decode front's rounding sequence)
+__device__ __forceinline__ u32 situ_bf16x2(float g_lo, float g_hi, float u_lo, float u_hi) {
+  const float2 g = bf16x2_to_f2(f2_to_bf16x2(g_lo, g_hi)), u = bf16x2_to_f2(f2_to_bf16x2(u_lo, u_hi));
+  return f2_to_bf16x2(situ_front(g.x, u.x), situ_front(g.y, u.y));
+}
+
 // Byte offset of row r's 16-byte chunk k (8 bf16) in a K-major operand of 128-byte swizzle atoms, 64-row
 // atom columns 8 KB apart (the tensor core's SWIZZLE_128B pattern: chunk index XOR row mod 8).
 __device__ __forceinline__ u32 front_swizzle(int r, int k) {
@@ -664,76 +677,68 @@ __device__ __forceinline__ void front_work_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(dropin::F_WORKERS) : "memory");
 }
 
-// The last row block's routing tables over the T x 16 picks, thread i the pick i = row * 16 + k: a pick's
-// slot within its expert is the number of earlier picks of that expert (warp counts, then ranks inside the
-// warp by __match_any_sync), so an expert's rows come in token order.  Scratch in the (otherwise unused)
-// dynamic shared memory.
-__device__ __forceinline__ void front_tables(const int* __restrict__ idx, int first, int T, int* __restrict__ scratch,
+// The last row block's routing tables over the T x 16 picks, thread i the pick i = row * 16 + k.  An
+// expert's rows are kept as a 64-bit mask of the picking rows (T <= 64; a row picks an expert at most once),
+// so its count is a popcount and a pick's slot within the expert is the number of picking rows before its
+// own: an expert's rows come in token order.  Scratch in the (otherwise unused) dynamic shared memory, the
+// masks zeroed by the caller.
+__device__ __forceinline__ void front_tables(const int* __restrict__ idx, int first, int T, u64* __restrict__ scratch,
                                              int* __restrict__ cta_batch, int* __restrict__ cta_limit,
                                              int* __restrict__ num_non_exiting, int* __restrict__ total_padded,
                                              int* __restrict__ route_map, int* __restrict__ exp2perm) {
   using namespace dropin;
-  int* wcnt = scratch;                 // [32 warps][F_LOCAL]: picks of each expert a warp, then their offsets
-  int* cnt = wcnt + 32 * F_LOCAL;      // [F_LOCAL]
-  int* off = cnt + F_LOCAL;            // [F_LOCAL + 1] first CTA of each expert
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  for (int i = t; i < 32 * F_LOCAL; i += F_THREADS) wcnt[i] = 0;
+  u64* rows = scratch;                                   // [F_LOCAL] the rows picking each expert
+  int* off = reinterpret_cast<int*>(rows + F_LOCAL);     // [F_LOCAL + 1] first CTA of each expert
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, r = t / TOPK;
   int j = -1;
   if (t < T * TOPK) {
     const int d = __ldcg(idx + t) - first;
     if (d >= 0 && d % F_STRIDE == 0 && d / F_STRIDE < F_LOCAL) j = d / F_STRIDE;
   }
+  if (j >= 0) atomicOr(rows + j, 1ull << r);  // rows[] zeroed by the caller before its last barrier
   __syncthreads();
-  const u32 same = __match_any_sync(0xffffffffu, j);
-  const int before = __popc(same & ((1u << lane) - 1u));
-  if (j >= 0 && before == 0) wcnt[warp * F_LOCAL + j] = __popc(same);
-  __syncthreads();
-  for (int e = warp; e < F_LOCAL; e += 32) {  // an expert a warp, lane w holding warp w's count
-    const int v = wcnt[lane * F_LOCAL + e];
-    int incl = v;
+  if (warp == 0) {  // off: exclusive scan of the experts' CTA counts, EPL consecutive experts a lane
+    constexpr int EPL = (F_LOCAL + 31) / 32;
+    int ctas[EPL], sum = 0;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+      const int e = lane * EPL + k;
+      ctas[k] = e < F_LOCAL ? (__popcll(rows[e]) + F_TILE - 1) / F_TILE : 0;
+      sum += ctas[k];
+    }
+    int incl = sum;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, incl, d);
       if (lane >= d) incl += y;
     }
-    wcnt[lane * F_LOCAL + e] = incl - v;
-    if (lane == 31) cnt[e] = incl;
-  }
-  __syncthreads();
-  if (warp == 0) {  // off: exclusive scan of the experts' CTA counts, 32 experts a round
-    int carry = 0;
-    for (int e0 = 0; e0 < F_LOCAL; e0 += 32) {
-      const int e = e0 + lane;
-      const int ctas = e < F_LOCAL ? (cnt[e] + F_TILE - 1) / F_TILE : 0;
-      int incl = ctas;
+    int run = incl - sum;
 #pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += y;
-      }
-      if (e < F_LOCAL) off[e] = carry + incl - ctas;
-      carry += __shfl_sync(0xffffffffu, incl, 31);
+    for (int k = 0; k < EPL; ++k) {
+      const int e = lane * EPL + k;
+      if (e < F_LOCAL) off[e] = run;
+      run += ctas[k];
     }
-    if (lane == 0) {
-      off[F_LOCAL] = carry;
-      num_non_exiting[0] = carry;
-      total_padded[0] = carry * F_TILE;
+    if (lane == 31) {
+      off[F_LOCAL] = incl;
+      num_non_exiting[0] = incl;
+      total_padded[0] = incl * F_TILE;
     }
   }
   __syncthreads();
   if (t < F_LOCAL) {
-    const int o0 = off[t], o1 = off[t + 1], lim = o0 * F_TILE + cnt[t];
+    const int o0 = off[t], o1 = off[t + 1], lim = o0 * F_TILE + __popcll(rows[t]);
     for (int c = o0; c < o1; ++c) {
       cta_batch[c] = t;
       cta_limit[c] = min((c + 1) * F_TILE, lim);
     }
-    for (int r = lim; r < o1 * F_TILE; ++r) route_map[r] = 0;
+    for (int p = lim; p < o1 * F_TILE; ++p) route_map[p] = 0;
   }
   if (t < T * TOPK) {
     int row = -1;
     if (j >= 0) {
-      row = off[j] * F_TILE + wcnt[warp * F_LOCAL + j] + before;
-      route_map[row] = t / TOPK;
+      row = off[j] * F_TILE + __popcll(rows[j] & ((1ull << r) - 1ull));
+      route_map[row] = r;
     }
     exp2perm[t] = row;
   }
@@ -794,10 +799,11 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
     int* __restrict__ route_map, int* __restrict__ exp2perm, const bf16* __restrict__ wsh, bf16* __restrict__ sh_out,
     const uint8_t* __restrict__ w13, const uint8_t* __restrict__ w13_sf, int first, int T) {
   using namespace k3::dropin;
-  extern __shared__ uint8_t f_dyn[];
+  extern __shared__ __align__(16) uint8_t f_dyn[];
   __shared__ int s_last, s_fail;
   __shared__ u32 s_tmem;
   __shared__ __align__(8) u64 s_bar;
+  __shared__ __align__(8) u64 s_wbar;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -820,8 +826,9 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
     int* c_e = reinterpret_cast<int*>(c_key + F_EXPERTS);           // [F_EXPERTS]
     u32* s_wmax = reinterpret_cast<u32*>(c_e + F_EXPERTS);          // [32]
     int* s_pick = reinterpret_cast<int*>(s_wmax + 32);              // [TOPK]
-    int* s_n = s_pick + TOPK;
-    int* table_scratch = s_n + 32;
+    int* s_n = s_pick + TOPK;                                       // [1] candidates
+    int* s_ccnt = s_n + 16;                                         // [32] candidates a warp (16-byte aligned)
+    u64* table_scratch = reinterpret_cast<u64*>(s_ccnt + 32);
     if (warp < F_SORT_WARPS) {
       // the latent's loads in flight from the start (quantised after the ranking)
       float4 lat_lo = make_float4(0.f, 0.f, 0.f, 0.f), lat_hi = lat_lo;
@@ -836,31 +843,41 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
       s_sig[t] = sg;
       const u32 m = __reduce_max_sync(0xffffffffu, key);
       if (lane == 0) s_wmax[warp] = m;
-      if (t == 0) *s_n = 0;
       asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
-      u32 v = lane < F_SORT_WARPS ? s_wmax[lane] : 0u;
+      // tau: lane l ranks warp l's maximum among all of them (ties by warp index); rank TOPK - 1 is tau
+      const u32 wm = lane < F_SORT_WARPS ? s_wmax[lane] : 0u;
+      int wrank = 0;
 #pragma unroll
-      for (int k = 2; k <= 32; k <<= 1)
+      for (int q4 = 0; q4 < F_SORT_WARPS / 4; ++q4) {
+        const uint4 m4 = reinterpret_cast<const uint4*>(s_wmax)[q4];
+        const u32 mq[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-          const u32 p = __shfl_xor_sync(0xffffffffu, v, j);
-          v = (((lane & k) == 0) == ((lane & j) == 0)) ? max(v, p) : min(v, p);  // descending
-        }
-      const u32 tau = __shfl_sync(0xffffffffu, v, TOPK - 1);
+        for (int h = 0; h < 4; ++h) wrank += (mq[h] > wm) | ((mq[h] == wm) & (4 * q4 + h < lane));
+      }
+      const u32 tau = __shfl_sync(0xffffffffu, wm, __ffs(__ballot_sync(0xffffffffu, wrank == TOPK - 1)) - 1);
+      // the candidates compacted in warp order: a warp's slots start after the lower warps' candidates
       const bool cand = key >= tau;
       const u32 bal = __ballot_sync(0xffffffffu, cand);
-      int at = 0;
-      if (lane == 0) at = atomicAdd(s_n, __popc(bal));
-      at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & ((1u << lane) - 1u));
+      if (lane == 0) s_ccnt[warp] = __popc(bal);
+      asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
+      int base = 0;
+#pragma unroll
+      for (int q4 = 0; q4 < F_SORT_WARPS / 4; ++q4) {
+        const int4 c4 = reinterpret_cast<const int4*>(s_ccnt)[q4];
+        base += (4 * q4 < warp ? c4.x : 0) + (4 * q4 + 1 < warp ? c4.y : 0) + (4 * q4 + 2 < warp ? c4.z : 0) +
+                (4 * q4 + 3 < warp ? c4.w : 0);
+      }
       if (cand) {
+        const int at = base + __popc(bal & ((1u << lane) - 1u));
         c_key[at] = key;
         c_e[at] = t;
       }
+      if (warp == F_SORT_WARPS - 1 && lane == 0) *s_n = base + __popc(bal);
       asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
-      if (warp < F_RANK_WARPS) {
+      {
         // candidate i's rank: the candidates with a larger key, or the same key and a smaller expert
         const int n = *s_n;
-        for (int i = warp; i < n; i += F_RANK_WARPS) {
+        for (int i = warp; i < n; i += F_SORT_WARPS) {
           const u32 ki = c_key[i];
           const int ei = c_e[i];
           int ahead = 0;
@@ -871,7 +888,32 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
           ahead = __reduce_add_sync(0xffffffffu, ahead);
           if (lane == 0 && ahead < TOPK) s_pick[ahead] = ei;
         }
-      } else {
+      }
+      asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
+      if (warp == 0) {
+        const int pick = lane < TOPK ? s_pick[lane] : 0;
+        // the row's two lowest local picks, to every shared-expert block's prefetcher (which the launch's
+        // end waits for), first
+        const int d = pick - first;
+        const int mine = lane < TOPK && d >= 0 && d % F_STRIDE == 0 ? d / F_STRIDE : F_LOCAL;
+        const int j = __reduce_min_sync(0xffffffffu, mine);
+        const int j2 = __reduce_min_sync(0xffffffffu, mine == j ? F_LOCAL : mine);
+        for (int c = lane; c < F_READERS; c += 32) st_relaxed_i32(ids + c * 64 + b, 1 + j + 256 * j2);
+        if (lane < TOPK) idx[(long long)b * TOPK + lane] = pick;
+        // warp 1 counts the row in once the picks are stored; this warp goes on with the weights
+        asm volatile("bar.arrive 4, 64;" ::: "memory");
+        const float w = lane < TOPK ? s_sig[pick] : 0.f;
+        float den = w;
+#pragma unroll
+        for (int off = TOPK / 2; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+        if (lane < TOPK) wts[(long long)b * TOPK + lane] = (w / (den + 1e-20f)) * rsv;
+      } else if (warp == 1) {
+        asm volatile("bar.sync 4, 64;" ::: "memory");
+        if (lane == 0) {  // the row's picks are out: count it in (release them, acquire the other rows')
+          const int n = atom_add_acq_rel(done, 1);
+          s_last = (n & F_COUNT) == T - 1;
+        }
+      } else if (warp >= F_RANK_WARPS) {
         // the latent: 8 columns a thread (four threads a 32-column group), landed to bf16, then MXFP8
         const uint4 lv = make_uint4(f2_to_bf16x2(lat_lo.x, lat_lo.y), f2_to_bf16x2(lat_lo.z, lat_lo.w),
                                     f2_to_bf16x2(lat_hi.x, lat_hi.y), f2_to_bf16x2(lat_hi.z, lat_hi.w));
@@ -879,29 +921,6 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
         const uint2 w = quant8_lanes(lv, sfb);
         reinterpret_cast<uint2*>(q + (long long)b * LATENT)[u] = w;
         if ((u & 3) == 0) sf[(long long)b * (LATENT / 32) + (u >> 2)] = (uint8_t)sfb;
-      }
-      asm volatile("bar.sync 2, %0;" ::"n"(F_SORT_WARPS * 32) : "memory");
-      if (warp == 0) {
-        const int pick = lane < TOPK ? s_pick[lane] : 0;
-        const float w = lane < TOPK ? s_sig[pick] : 0.f;
-        float den = w;
-#pragma unroll
-        for (int off = TOPK / 2; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-        if (lane < TOPK) {
-          wts[(long long)b * TOPK + lane] = (w / (den + 1e-20f)) * rsv;
-          idx[(long long)b * TOPK + lane] = pick;
-        }
-        // the row's two lowest local picks, to every shared-expert block's prefetcher
-        const int d = pick - first;
-        const int mine = lane < TOPK && d >= 0 && d % F_STRIDE == 0 ? d / F_STRIDE : F_LOCAL;
-        const int j = __reduce_min_sync(0xffffffffu, mine);
-        const int j2 = __reduce_min_sync(0xffffffffu, mine == j ? F_LOCAL : mine);
-        for (int c = lane; c < F_READERS; c += 32) st_relaxed_i32(ids + c * 64 + b, 1 + j + 256 * j2);
-        __syncwarp();
-        if (lane == 0) {  // this row's picks are out: count the row in (release them, acquire the others')
-          const int n = atom_add_acq_rel(done, 1);
-          s_last = (n & F_COUNT) == T - 1;
-        }
       }
     } else {
       // the shared expert's SiTU, 4 columns a thread, gate and up landed to bf16 first; every pass's loads
@@ -917,17 +936,16 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
         }
 #pragma unroll
       for (int p = 0; p < PASSES; ++p)
-        if (k0 + p * LANES < F_SITU_THREADS) {
-          const float2 g0 = bf16x2_to_f2(f2_to_bf16x2(g[p].x, g[p].y)), g1 = bf16x2_to_f2(f2_to_bf16x2(g[p].z, g[p].w));
-          const float2 u0 = bf16x2_to_f2(f2_to_bf16x2(u[p].x, u[p].y)), u1 = bf16x2_to_f2(f2_to_bf16x2(u[p].z, u[p].w));
-          const uint2 o = make_uint2(f2_to_bf16x2(situ_front(g0.x, u0.x), situ_front(g0.y, u0.y)),
-                                     f2_to_bf16x2(situ_front(g1.x, u1.x), situ_front(g1.y, u1.y)));
-          reinterpret_cast<uint2*>(act + (long long)b * F_SH)[k0 + p * LANES] = o;
-        }
+        if (k0 + p * LANES < F_SITU_THREADS)
+          reinterpret_cast<uint2*>(act + (long long)b * F_SH)[k0 + p * LANES] =
+              make_uint2(situ_bf16x2(g[p].x, g[p].y, u[p].x, u[p].y), situ_bf16x2(g[p].z, g[p].w, u[p].z, u[p].w));
+      if (k0 < F_LOCAL) table_scratch[k0] = 0ull;  // the tables' expert masks, should this block be the last
       // the row is in: one flag to each shared-expert block (a release after the barrier: cumulative over
-      // the SiTU warps' stores)
-      asm volatile("bar.sync 3, %0;" ::"n"(LANES) : "memory");
-      for (int c = k0; c < F_READERS; c += LANES) st_release_i32(ready + c * 64 + b, 1);
+      // the SiTU warps' stores), unless those blocks compute the rows themselves
+      if (T > F_LOCAL_SITU_ROWS) {
+        asm volatile("bar.sync 3, %0;" ::"n"(LANES) : "memory");
+        for (int c = k0; c < F_READERS; c += LANES) st_release_i32(ready + c * 64 + b, 1);
+      }
     }
     __syncthreads();
     if (!s_last) return;
@@ -948,41 +966,88 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
   uint8_t* sa = sw + F_OPERAND;                                       // the T act rows
   bf16* tile = reinterpret_cast<bf16*>(sa + F_OPERAND);               // out [T][64]
   const u32 sw_at = smem_u32(sw), sa_at = smem_u32(sa);
-  for (int i = t; i < 64 * (F_SH / 8); i += F_WORKERS) {  // the weights need no flag: in flight at once
-    const int r = i / (F_SH / 8), k = i % (F_SH / 8);
-    cp_async16(sw_at + front_swizzle(r, k), wsh + (long long)(n0 + r) * F_SH + k * 8);
+  // Few rows: every block computes the act rows itself from the front GEMM's gate | up (bit for bit as the
+  // row blocks do), one 8-column chunk a thread, its loads in flight before anything else
+  const bool local_act = T <= F_LOCAL_SITU_ROWS;
+  const int ar = t / (F_SH / 8), ak = t % (F_SH / 8);
+  const bool my_chunk = local_act && t < T * (F_SH / 8);
+  float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0, u0 = g0, u1 = g0;
+  if (my_chunk) {
+    const float* gp = S + (long long)ar * F_LDS + F_EXPERTS + LATENT + ak * 8;
+    g0 = reinterpret_cast<const float4*>(gp)[0];
+    g1 = reinterpret_cast<const float4*>(gp)[1];
+    u0 = reinterpret_cast<const float4*>(gp + F_SH)[0];
+    u1 = reinterpret_cast<const float4*>(gp + F_SH)[1];
   }
   if (warp == 1) {
     tmem_alloc(&s_tmem, 64);
     tmem_relinquish();
   }
+  // Wsh's 64 rows (one contiguous 96 KB run).  With the act rows coming from the row blocks, the act region is
+  // needed for them: the rows go straight into the swizzled operand, 16 bytes a cp.async, in flight with the
+  // act rows' copies.  With few rows, one bulk copy (the TMA unit) stages them in the act region and the block
+  // swizzles them in shared memory, which lands them sooner.
+  if (!local_act)
+    for (int i = t; i < 64 * (F_SH / 8); i += F_WORKERS) {
+      const int r = i / (F_SH / 8), k = i % (F_SH / 8);
+      cp_async16(sw_at + front_swizzle(r, k), wsh + (long long)(n0 + r) * F_SH + k * 8);
+    }
   if (t == 0) {
     s_fail = 0;
+    mbar_init(&s_wbar, 1);
     mbar_init(&s_bar, 1);
     fence_mbar_init();
+    if (local_act) {
+      mbar_arrive_expect_tx(&s_wbar, (u32)F_OPERAND);
+      bulk_load(sa, wsh + (long long)n0 * F_SH, (u32)F_OPERAND, &s_wbar);
+    }
   }
   front_work_sync();
-  if (t < T) {
-    int* flag = ready + c * 64 + t;
-    if (wait_nonzero<true>(flag) != 0) {
-      *flag = 0;
+  if (local_act) {
+    if (mbar_wait(&s_wbar, 0, nullptr, nullptr, 0, F_WAIT_NS)) {
+      // the staged rows into the swizzled K-major operand, 16 bytes a step (conflict-free both ways)
+      constexpr int CHUNKS = 64 * (F_SH / 8), PER = (CHUNKS + F_WORKERS - 1) / F_WORKERS;
+      uint4 v[PER];
+#pragma unroll
+      for (int m = 0; m < PER; ++m)
+        if (t + m * F_WORKERS < CHUNKS) v[m] = reinterpret_cast<const uint4*>(sa)[t + m * F_WORKERS];
+#pragma unroll
+      for (int m = 0; m < PER; ++m) {
+        const int i = t + m * F_WORKERS;
+        if (i < CHUNKS) *reinterpret_cast<uint4*>(sw + front_swizzle(i / (F_SH / 8), i % (F_SH / 8))) = v[m];
+      }
     } else {
       s_fail = 1;
       atomicOr(done, F_ERR);
     }
-  }
-  front_work_sync();
-  const bool fail = *reinterpret_cast<volatile int*>(&s_fail) != 0;
-  if (!fail)
-    for (int i = t; i < T * (F_SH / 8); i += F_WORKERS) {
-      const int r = i / (F_SH / 8), k = i % (F_SH / 8);
-      cp_async16(sa_at + front_swizzle(r, k), act + (long long)r * F_SH + k * 8);
+    front_work_sync();  // the staging area read out: the act rows may land there
+    if (my_chunk)
+      *reinterpret_cast<uint4*>(sa + front_swizzle(ar, ak)) =
+          make_uint4(situ_bf16x2(g0.x, g0.y, u0.x, u0.y), situ_bf16x2(g0.z, g0.w, u0.z, u0.w),
+                     situ_bf16x2(g1.x, g1.y, u1.x, u1.y), situ_bf16x2(g1.z, g1.w, u1.z, u1.w));
+  } else {
+    if (t < T) {
+      int* flag = ready + c * 64 + t;
+      if (wait_nonzero<true>(flag) != 0) {
+        *flag = 0;
+      } else {
+        s_fail = 1;
+        atomicOr(done, F_ERR);
+      }
     }
-  cp_async_wait_all();
-  fence_proxy_async_shared();  // the operands, to the tensor core's reads
+    front_work_sync();
+    if (!*reinterpret_cast<volatile int*>(&s_fail))
+      for (int i = t; i < T * (F_SH / 8); i += F_WORKERS) {
+        const int r = i / (F_SH / 8), k = i % (F_SH / 8);
+        cp_async16(sa_at + front_swizzle(r, k), act + (long long)r * F_SH + k * 8);
+      }
+    cp_async_wait_all();
+  }
+  fence_proxy_async_shared();  // both operands (generic-proxy writes), to the tensor core's reads
   tc_fence_before();
   front_work_sync();
   tc_fence_after();
+  const bool fail = *reinterpret_cast<volatile int*>(&s_fail) != 0;
   const int tiles = (T + 7) / 8;
   if (!fail) {
     if (t == 0) {
@@ -1010,12 +1075,13 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
     }
   }
   tc_fence_before();
+  cp_async_wait_all();  // nothing of this block's in flight past here
   front_work_sync();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(s_tmem, 64);
   }
-  if (!fail)
+  if (!*reinterpret_cast<volatile int*>(&s_fail))
     for (int i = t; i < T * 8; i += F_WORKERS) {
       const int r = i >> 3, col = i & 7;
       reinterpret_cast<uint4*>(sh_out + (long long)r * F_NSH + n0)[col] = reinterpret_cast<const uint4*>(tile + r * 64)[col];
