@@ -350,3 +350,55 @@ def test_decode_front(dev, front_weights, ties):
         want = act_g.astype(np.float32) @ wsh.numpy().T
         got_sh = g["sh_out"].float().numpy()
         assert np.allclose(got_sh, want, rtol=1e-2, atol=2e-2 * np.abs(want).max()), f"{tag}: projection"
+
+
+def test_decode_front_latency(dev, front_weights, capsys):
+    """Device time of kern_k3_moe_front against the reference entry, 40 back-to-back launches a CUDA graph
+    (the step's launches, S resident in L2 as the front GEMM leaves it), best of 9 replays; printed, not
+    asserted (the numbers are quoted in the design notes).  Carries must be zero after every replay."""
+    wsh, w13, w13_sf = front_weights
+    rows = []
+    for T in (1, 8, 16, 32, 64):
+        S, bias = _front_inputs(T, 0, 500 + T, dev)
+        line = [T]
+        for module in ("k3_moe_front", MOD):
+            f = rk.function(module, "kern_k3_moe_front")
+            rk.allow_smem(f, FRONT_SMEM)
+            ready = torch.zeros(FRONT_READERS * 64, dtype=torch.int32, device=dev)
+            ids = torch.zeros_like(ready)
+            done = torch.zeros(1, dtype=torch.int32, device=dev)
+            S_d, b_d = _t(S, dev), _t(bias, dev)
+            rs = _t(np.array([0x4020], np.uint16), dev).view(torch.bfloat16)
+            o = [torch.zeros(n, dtype=torch.int32, device=dev) for n in
+                 (T * TOPK, T * TOPK, T * LATENT // 4, T * LATENT // 128, T * FRONT_SH // 2, FRONT_CTAS, FRONT_CTAS,
+                  1, 1, FRONT_CTAS * FRONT_TILE, T * TOPK, T * FRONT_NSH // 2)]
+            args = [rk.P(S_d), rk.P(b_d), rk.P(rs)] + [rk.P(x) for x in o[:5]] + [rk.P(ready), rk.P(ids), rk.P(done)] + \
+                   [rk.P(x) for x in o[5:11]] + [rk.P(wsh), rk.P(o[11]), rk.P(w13), rk.P(w13_sf), rk.I(0), rk.I(T)]
+            grid = (T + FRONT_READERS, 1, 1)
+            for _ in range(3):
+                rk.launch(f, grid, (1024, 1, 1), args, smem=FRONT_SMEM)
+            torch.cuda.synchronize()
+            side = torch.cuda.Stream()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(g, stream=side):
+                    for _ in range(40):
+                        rk.launch(f, grid, (1024, 1, 1), args, smem=FRONT_SMEM)
+            g.replay()
+            torch.cuda.synchronize()
+            best = float("inf")
+            for _ in range(9):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                e1.synchronize()
+                best = min(best, e0.elapsed_time(e1) * 1e3 / 40)
+            g.reset()
+            assert int(done.item()) == 0 and int(ready.abs().sum()) == 0 and int(ids.abs().sum()) == 0, module
+            line.append(best)
+        rows.append(line)
+    with capsys.disabled():
+        print("\nkern_k3_moe_front device time a launch (us): rows, reference, k3moe")
+        for T, r, k in rows:
+            print(f"  {T:3d}  {r:7.2f}  {k:7.2f}")
