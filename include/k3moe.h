@@ -126,8 +126,9 @@ int k3moe_quant_permute(const void* x_bf16, int ldx, int R, int cols, int K, con
  *   h = silu(g) * u, requantised to MXFP8 (the rule above) into
  *   fc1_q [cap, I] / fc1_sf (tiled over permuted rows).
  * FC2: fc2 [cap, H] bf16 = W2_e . fc1 over each tile's rows.
- * Tables from k3moe_route_tables (tile 128).  H, I multiples of 256; err:
- * the device error words (2 x u32).
+ * Tables from k3moe_route_tables (tile 128).  H, I multiples of 256; fc1_q
+ * and fc2_bf16 32-byte aligned (K3MOE_EINVAL otherwise); err: the device
+ * error words (2 x u32).
  * Replaces: the FC1 / FC2 batched GEMMs (kernels.toml:1-9; arguments
  *   scripts/k3_moe_bmm.py:131-134, 167-169; docs/k3-kernel-abi.md:535-565). */
 int k3moe_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,

@@ -105,6 +105,9 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   if (H <= 0 || I <= 0 || H % 256 || I % 256 || n_experts <= 0 || cap_rows <= 0 || cap_rows % 128 || max_ctas <= 0 ||
       (long long)max_ctas * 128 > cap_rows)
     return K3MOE_EINVAL;
+  // the epilogues store 32 bytes at a time (256-bit stores): the outputs must start 32-byte aligned
+  const void* out0 = mode == MODE_FC1 ? static_cast<const void*>(out_q) : out_bf16;
+  if (out0 == nullptr || reinterpret_cast<uintptr_t>(out0) % 32 != 0) return K3MOE_EINVAL;
   const int K = mode == MODE_FC1 ? H : I;
   const int rows_per_expert = mode == MODE_FC1 ? 2 * I : H;
   CUtensorMap ta, tb;

@@ -369,9 +369,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
               q[j] = (u32)e4m3x2_sat(hv[4 * j] * s, hv[4 * j + 1] * s) |
                      ((u32)e4m3x2_sat(hv[4 * j + 2] * s, hv[4 * j + 3] * s) << 16);
             const int f = w.fb * 128 + 64 * half + 32 * g;
-            uint4* dst = reinterpret_cast<uint4*>(p.out_q + op8_offset(r, f, p.out_cols));
-            dst[0] = make_uint4(q[0], q[1], q[2], q[3]);
-            dst[1] = make_uint4(q[4], q[5], q[6], q[7]);
+            st_global_v8(p.out_q + op8_offset(r, f, p.out_cols), q);  // the group's 32 bytes, contiguous
             sfw |= (u32)(e + 127) << (8 * g);
           }
           // the two groups' scales are adjacent bytes of one atom row (kb even)
@@ -383,13 +381,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              uint4 o;
-              o.x = f2_to_bf16x2(__uint_as_float(v[q][j]), __uint_as_float(v[q][j + 1]));
-              o.y = f2_to_bf16x2(__uint_as_float(v[q][j + 2]), __uint_as_float(v[q][j + 3]));
-              o.z = f2_to_bf16x2(__uint_as_float(v[q][j + 4]), __uint_as_float(v[q][j + 5]));
-              o.w = f2_to_bf16x2(__uint_as_float(v[q][j + 6]), __uint_as_float(v[q][j + 7]));
-              *reinterpret_cast<uint4*>(dst + 32 * q + j) = o;
+            for (int j = 0; j < 32; j += 16) {  // 16 columns, 32 bytes a store
+              u32 o[8];
+#pragma unroll
+              for (int h = 0; h < 8; ++h)
+                o[h] = f2_to_bf16x2(__uint_as_float(v[q][j + 2 * h]), __uint_as_float(v[q][j + 2 * h + 1]));
+              st_global_v8(dst + 32 * q + j, o);
             }
           }
         }
