@@ -565,6 +565,67 @@ def run_decode(args, world, rank, dev):
 
 
 # ------------------------------------------------------------------ the GPU arm
+def run_native(args, dev):
+    """The layer at the reference's own shapes (K3: latent 3584, I 3072, top-16, SiTU gate, 896 experts, the
+    shared expert outside the MoE kernels as in the reference's P step), 8192 rows on one GPU: the workload of
+    the reference's published P MoE layer time (route + FC1 + FC2 + finalize, roofline/prefill.md:101, measured
+    on GB300).  One JSON line; ms a layer, lower is better."""
+    import torch
+
+    import k3moe
+
+    Hn, In, En, Kn, T = 3584, 3072, 896, 16, args.tokens
+    k3moe.lib()
+    w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, En * 2 * In, Hn, WSD, device=dev)
+    w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, En * Hn, In, WSD, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000)
+    x = torch.randn((T, Hn), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    g.manual_seed(7)
+    wr = torch.randn((Hn, En), generator=g, device=dev, dtype=torch.float32) / Hn ** 0.5
+    S = (x.float() @ wr).contiguous()
+    bias = (torch.rand(En, generator=g, device=dev) * 0.2 - 0.1).float()
+    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
+    del wr
+    layer = k3moe.MoELayer(Hn, In, En, Kn, 0, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev,
+                           activation=k3moe.ACT_SITU)
+    out = torch.empty((T, Hn), dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup):
+        layer.forward(S, x, out)
+    torch.cuda.synchronize()
+    layer.check_device_error(T)
+    stream = torch.cuda.current_stream()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+    for row in ev:
+        for e in row:
+            e.record(stream)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    torch.cuda.synchronize()
+    with ClockSampler(uuid) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            layer.forward_events(S, x, out, ev[s])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    layer.check_device_error(T)
+    ms = start.elapsed_time(stop) / args.steps
+    stage_ms = np.array([[ev[s][i].elapsed_time(ev[s][i + 1]) for i in range(6)] for s in range(args.steps)]).mean(0)
+    flops = 2.0 * T * Kn * (Hn * 2 * In + In * Hn)
+    line = {"metric": "MoE layer ms @8192-row prefill, K3 native shape", "value": ms, "unit": "ms/layer",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+            "tokens_per_s": T / (ms / 1e3), "tflops": flops / (ms / 1e3) / 1e12, "dtype": "mxfp8 x mxfp4 (f32 accumulate)",
+            "data": "synthetic", "stage_ms": dict(zip(["topk", "tables", "permute", "fc1", "fc2", "combine"],
+                                                      [round(float(v), 4) for v in stage_ms])),
+            "config": {"workload": "K3 native-shape prefill MoE layer (latent 3584, I 3072, top-16, SiTU, no shared)",
+                       "T": T, "H": Hn, "I": In, "E": En, "K": Kn, "shared_expert_width": 0, "rs": RS,
+                       "parallelism": "ep1", "l2": "inputs larger than L2: 15.7 GB of expert weights"},
+            "reference_published": {"value": 4.76, "unit": "ms/layer", "hardware": "GB300 (sm_103a, 1400 W)",
+                                    "source": "roofline/prefill.md:101 (52.37 ms per 11 layers)"},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -582,6 +643,8 @@ def main():
                     help="N > 1: experts dealt to ranks by router bias (balanced) or in contiguous blocks")
     ap.add_argument("--zipf", action="store_true",
                     help="config 3: the routing bias makes expert popularity Zipf(1.1) (N = 1 prefill)")
+    ap.add_argument("--native", action="store_true",
+                    help="the layer at the reference's own K3 shapes (latent 3584, I 3072, top-16, SiTU), N = 1")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -603,6 +666,8 @@ def main():
         return run_decode(args, world, rank, dev) if args.decode else run_ep(args, world, rank, dev)
     if args.decode:
         return run_decode(args, world, rank, dev)
+    if args.native:
+        return run_native(args, dev)
     E = args.experts  # noqa: N806  (the routed experts of this run; smaller only for profiling captures)
     T = args.tokens
     k3moe.lib()
