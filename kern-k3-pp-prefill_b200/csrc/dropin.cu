@@ -528,9 +528,10 @@ extern "C" __global__ void kern_k3_moe_sf_shuffle(const uint8_t* __restrict__ sr
 // memory, launched as a programmatic dependent of the front GEMM (it waits at entry, then releases FC1).
 //   row block b < T   top-16 of the router columns (idx, wts: kern_k3g_router_topk's picks and bits); the
 //                     latent landed to bf16 and quantised to MXFP8 with linear scales (q, sf:
-//                     kern_k3_moe_quant's bytes); the shared expert's SiTU row (act); a flag to every
-//                     shared-expert block once the act row is in (ready), and the row's two lowest local
-//                     picks to their prefetchers (ids); the last row block to arrive (done) builds the
+//                     kern_k3_moe_quant's bytes); the shared expert's SiTU row (act); with more than
+//                     F_LOCAL_SITU_ROWS rows a flag to every shared-expert block once the act row is in
+//                     (ready), and always the row's two lowest local picks to the shared-expert blocks'
+//                     prefetchers (ids); the last row block to arrive (done) builds the
 //                     routing tables of this rank's experts first + j * STRIDE (j < EXPERTS / STRIDE), TILE
 //                     rows a CTA, an expert's rows in token order (the reference leaves them in atomic order;
 //                     the GEMMs compute each row on its own), padding rows routing token 0, exp2perm -1 for
@@ -595,9 +596,10 @@ static_assert(F_LOCAL <= F_THREADS - F_SORT_WARPS * 32 && F_MAX_ROWS * TOPK <= F
 static_assert(F_MAX_ROWS <= 64, "an expert's picking rows fit a 64-bit mask");
 static_assert(F_SORT_WARPS % 4 == 0, "warp maxima read four at a time");
 
+// Up to this many rows every shared-expert block computes the SiTU rows itself instead of waiting for the row
+// blocks' flags (and stages its weight rows with one bulk copy)
 constexpr int F_LOCAL_SITU_ROWS = 8;
-static_assert(F_LOCAL_SITU_ROWS * (F_SH / 8) <= F_WORKERS, "one act chunk a thread");  // up to this many rows every shared-expert block computes the SiTU rows
-                                       // itself instead of waiting for the row blocks' flags
+static_assert(F_LOCAL_SITU_ROWS * (F_SH / 8) <= F_WORKERS, "one act chunk a thread");
 static_assert(F_RANK_WARPS >= 2 && F_SORT_WARPS <= 31 && F_SORT_WARPS >= TOPK,
               "ranking warps, a warp left for the SiTU, at least TOPK warp maxima");
 static_assert(F_SH % 64 == 0 && F_NSH % 64 == 0 && F_LDS % 4 == 0, "whole swizzle atoms, 16-byte rows");
