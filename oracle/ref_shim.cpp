@@ -11,4 +11,8 @@ int k3ref_topk(void) { return k3ref::TOPK; }
 void k3ref_router_topk(const float* S, const float* bias, const uint16_t* rs, int* idx, float* wts, int B) {
   k3ref::ref_router_topk(S, bias, rs, idx, wts, B);
 }
+// ref_land_situ: p f32 [B, 2n] (gate | up) -> act bf16 [B, n], K3's SiTU with bf16 landings
+void k3ref_land_situ(const float* p, uint16_t* act, int n, int B) {
+  k3ref::ref_land_situ(p, act, n, B);
+}
 }

@@ -33,6 +33,17 @@ def inputs(B, seed):
 
 
 RS_BITS = 0x4020  # bf16 2.5
+SITU_ROWS, SITU_N = 4, 768
+
+
+def situ_inputs():
+    rng = np.random.default_rng(4242)
+    p = np.empty((SITU_ROWS, 2 * SITU_N), np.float32)
+    p[:, :SITU_N] = rng.uniform(-12, 12, (SITU_ROWS, SITU_N))
+    p[:, SITU_N:] = rng.uniform(-60, 60, (SITU_ROWS, SITU_N))
+    p[0, :16] = 0.0
+    p[1, SITU_N:SITU_N + 16] = 0.0
+    return p
 
 
 def main():
@@ -51,6 +62,17 @@ def main():
         out[f"wts_{B}"] = wts
     np.savez_compressed(os.path.join(HERE, "router_topk_ref.npz"), **out)
     print("wrote", os.path.join(HERE, "router_topk_ref.npz"))
+
+    # K3's shared-expert SiTU with its bf16 landings (harness/k3/ref.h:614-622, `ref_land_situ`): gate | up
+    # f32 rows of one rank's shared width (768), values spread over the tanh knees (|g| up to 12, |u| up to
+    # 60) plus exact zeros; regenerated from the seed, only the outputs stored
+    B, n = SITU_ROWS, SITU_N
+    p = situ_inputs()
+    act = np.empty((B, n), np.uint16)
+    lib.k3ref_land_situ(p.ctypes.data_as(ctypes.c_void_p), act.ctypes.data_as(ctypes.c_void_p), ctypes.c_int(n),
+                        ctypes.c_int(B))
+    np.savez_compressed(os.path.join(HERE, "land_situ_ref.npz"), act=act)
+    print("wrote", os.path.join(HERE, "land_situ_ref.npz"))
 
 
 if __name__ == "__main__":

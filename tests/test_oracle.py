@@ -51,6 +51,48 @@ def test_topk8_is_prefix_of_topk16():
     assert np.array_equal(idx8, g["idx_64"][:, :8])
 
 
+def test_situ_oracle_matches_reference_golden():
+    """oracle.situ (with the decode front's bf16 landings) against the reference's own CPU reference
+    `ref_land_situ` (harness/k3/ref.h:614-622), golden vectors from tests/golden/make_golden.py: bit-equal."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(HERE, "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    p = mg.situ_inputs()
+    n = mg.SITU_N
+    want = np.load(os.path.join(HERE, "golden", "land_situ_ref.npz"))["act"]
+    land = lambda a: oracle.bf16_to_f32(oracle.bf16_bits(a))  # noqa: E731
+    got = oracle.bf16_bits(oracle.situ(land(p[:, :n]), land(p[:, n:])).astype(np.float32))
+    assert np.array_equal(got, want)
+
+
+def test_strided_tables_slice_of_experts():
+    """The decode front's tables over a strided slice (experts first + j * stride): token order within an
+    expert, other ranks' picks -1, CTA rows of 16, padding rows routed to token 0."""
+    rng = np.random.default_rng(5)
+    T, K, E, stride, first = 24, 16, 896, 8, 3
+    idx = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    tb = oracle.strided_tables(idx, first, stride, E // stride, 16)
+    e2p = tb["exp2perm"]
+    mine = ((idx - first) >= 0) & ((idx - first) % stride == 0)
+    assert ((e2p >= 0) == mine).all()
+    rm, cb = tb["route_map"], tb["cta_batch"]
+    rows_of = {}
+    for t in range(T):
+        for k in range(K):
+            if e2p[t, k] >= 0:
+                j = (idx[t, k] - first) // stride
+                assert rm[e2p[t, k]] == t and cb[e2p[t, k] // 16] == j
+                rows_of.setdefault(j, []).append((e2p[t, k], t))
+    for j, rows in rows_of.items():  # an expert's rows in token order, from the start of its first CTA
+        rows.sort()
+        assert [t for _, t in rows] == sorted(t for _, t in rows)
+        assert rows[0][0] % 16 == 0
+    nne, tp = int(tb["meta"][0]), int(tb["meta"][1])
+    assert tp == 16 * nne and (rm[:tp] >= 0).all()
+
+
 def test_e4m3_codes_round_trip():
     lib = oracle.lib()
     for b in range(256):
