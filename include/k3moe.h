@@ -172,6 +172,28 @@ int k3moe_ep_ids(const uint8_t* rows, int stride, int R, int H, int32_t* ids, k3
 /* Packed row i -> permuted row perm[i] (>= 0) of the GEMM operand (tile-major q, tiled scales). */
 int k3moe_ep_unpack(const uint8_t* rows, int stride, int R, int H, const int32_t* perm, uint8_t* q_perm,
                     uint8_t* sf_perm, k3moe_stream_t stream);
+/* Per-destination rows (the counts-exchange dispatch): a token travels once to
+ * each rank holding any of its picks, as E4M3 [H] | UE8M0 [H/32] | int16 [K]
+ * local expert ids of its picks there (pick order, -1 after), stride
+ * k3moe_ep_pair_row_stride(H, K).  The receiver routes a row to all its
+ * experts and returns FC2's results one row a pick, so k3moe_combine_ep is
+ * unchanged.  W (ranks) <= 32. */
+int k3moe_ep_pair_row_stride(int H, int K);
+/* pair_ids[t*W + d] = d when token t has a pick on rank d (dest[t*K + k] == d), else -1. */
+int k3moe_ep_pairs(const int32_t* dest, int T, int K, int W, int32_t* pair_ids, k3moe_stream_t stream);
+/* Quantise row t once; write it to slot pair_pos[t*W + d] (>= 0) of every rank d it goes to, headed by
+ * lid[t*K + k] for its picks with dest[t*K + k] == d; with pair_pos null, to slot t headed by fixed_eid. */
+int k3moe_ep_pack_pairs(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* dest, const int32_t* lid,
+                        const int32_t* pair_pos, int W, int fixed_eid, uint8_t* dst, int stride,
+                        k3moe_stream_t stream);
+/* ids[i*K + j] = the j-th local expert id of per-destination row i (-1 none). */
+int k3moe_ep_ids_k(const uint8_t* rows, int stride, int R, int H, int K, int32_t* ids, k3moe_stream_t stream);
+/* Per-destination row i -> permuted rows perm[i*K + j] (>= 0) of the GEMM operand. */
+int k3moe_ep_unpack_k(const uint8_t* rows, int stride, int R, int H, int K, const int32_t* perm, uint8_t* q_perm,
+                      uint8_t* sf_perm, k3moe_stream_t stream);
+/* out_rows[perm[i*K + j]] = the (i, j) pair's number among the valid pairs in (i, j) order: the return row of
+ * FC2's result (k3moe_fc2_to_rows). */
+int k3moe_ep_return_rows(const int32_t* perm, int R, int K, int32_t* out_rows, k3moe_stream_t stream);
 /* out[t] = bf16( sum_k fma(wts[t,k], back[pos[t,k]], acc) (pos >= 0, k in order) + shared[t] ):
  * the combine over rows returned by the combine all-to-all (shared_bf16 may be null). */
 int k3moe_combine_ep(const void* back_bf16, const int32_t* pos, const float* wts, const void* shared_bf16,

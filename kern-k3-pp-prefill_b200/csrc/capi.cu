@@ -421,6 +421,61 @@ int k3moe_ep_unpack(const uint8_t* rows, int stride, int R, int H, const int32_t
   return launch_status();
 }
 
+int k3moe_ep_pair_row_stride(int H, int K) {
+  return H > 0 && H % 256 == 0 && K >= 1 && K <= 16 ? (H + H / 32 + 2 * K + 15) / 16 * 16 : 0;
+}
+
+int k3moe_ep_pairs(const int32_t* dest, int T, int K, int W, int32_t* pair_ids, k3moe_stream_t stream) {
+  if (T < 0 || K < 1 || K > 16 || W < 1 || W > 32 || !dest || !pair_ids) return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  const int grid = (int)std::min<long long>(cdiv(T, 256), (long long)num_sms(current_device()) * 4);
+  ep_pairs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(dest, T, K, W, pair_ids);
+  return launch_status();
+}
+
+int k3moe_ep_pack_pairs(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* dest, const int32_t* lid,
+                        const int32_t* pair_pos, int W, int fixed_eid, uint8_t* dst, int stride,
+                        k3moe_stream_t stream) {
+  if (T < 0 || H <= 0 || H % 256 || ldx < H || ldx % 8 || K < 1 || K > 16 || !dst ||
+      stride < k3moe_ep_pair_row_stride(H, K) || stride % 16 || (pair_pos && (W < 1 || W > 32 || !dest || !lid)) ||
+      (!pair_pos && (fixed_eid < -32768 || fixed_eid > 32767)))
+    return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  const int sms = num_sms(current_device());
+  const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
+  const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
+  ep_pack_pairs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, fixed_eid, dst, stride, split);
+  return launch_status();
+}
+
+int k3moe_ep_ids_k(const uint8_t* rows, int stride, int R, int H, int K, int32_t* ids, k3moe_stream_t stream) {
+  if (R < 0 || H <= 0 || H % 256 || K < 1 || K > 16 || stride < k3moe_ep_pair_row_stride(H, K)) return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  const long long n = (long long)R * K;
+  const int grid = (int)std::min<long long>(cdiv(n, 256), (long long)num_sms(current_device()) * 8);
+  ep_ids_k_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(rows, stride, R, H, K, ids);
+  return launch_status();
+}
+
+int k3moe_ep_unpack_k(const uint8_t* rows, int stride, int R, int H, int K, const int32_t* perm, uint8_t* q_perm,
+                      uint8_t* sf_perm, k3moe_stream_t stream) {
+  if (R < 0 || H <= 0 || H % 256 || K < 1 || K > 16 || stride < k3moe_ep_pair_row_stride(H, K) || stride % 16)
+    return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  const int grid = (int)std::min<long long>(cdiv(R, 8), (long long)num_sms(current_device()) * 8);
+  ep_unpack_k_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(rows, stride, R, H, K, perm, q_perm,
+                                                                               sf_perm);
+  return launch_status();
+}
+
+int k3moe_ep_return_rows(const int32_t* perm, int R, int K, int32_t* out_rows, k3moe_stream_t stream) {
+  if (R < 0 || K < 1 || K > 16 || !perm || !out_rows) return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  ep_return_rows_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(perm, R, K, out_rows);
+  return launch_status();
+}
+
 int k3moe_combine_ep(const void* back_bf16, const int32_t* pos, const float* wts, const void* shared_bf16,
                      int ld_shared, void* out_bf16, int ldo, int T, int K, int cols, k3moe_stream_t stream) {
   if (T < 0 || K < 1 || K > 16 || cols <= 0 || cols % 8 || ldo < cols || ldo % 8 ||

@@ -9,9 +9,162 @@
 //   [H, H + H/32)     UE8M0 scale per 32 elements, linear
 //   [H + H/32, +4)    local expert id at the destination (int32)
 //   the rest          unused (rows stay 16-byte aligned)
+//
+// Per-destination rows (the counts-exchange dispatch): a token is sent once to each rank holding any of its
+// picks, stride roundup(H + H/32 + 2 K, 16):
+//   [0, H + H/32)     as above
+//   [H + H/32, +2K)   the local expert ids (int16) of the token's picks on that rank, in pick order, -1 after
+// The receiver routes each row to all its experts; FC2's results go back one row a pick, in (token, pick)
+// order, so the owner's combine is unchanged.
 #include "common.cuh"
 
 namespace k3 {
+
+// pair_ids[t*W + d] = d when token t has a pick on rank d, else -1 (W <= 64)
+__global__ void __launch_bounds__(256) ep_pairs_kernel(const int* __restrict__ dest, int T, int K, int W,
+                                                       int* __restrict__ pair_ids) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+    unsigned long long on = 0ull;
+    for (int k = 0; k < K; ++k) {
+      const int d = dest[(long long)t * K + k];
+      if (d >= 0 && d < W) on |= 1ull << d;
+    }
+    for (int d = 0; d < W; ++d) pair_ids[(long long)t * W + d] = ((on >> d) & 1ull) ? d : -1;
+  }
+}
+
+// `split` warps a source row: quantise token t once and write it to the slot pair_pos[t*W + d] of every rank d
+// it goes to, headed by the local ids of its picks there (lid[t*K + k] where dest[t*K + k] == d, in k order);
+// with pair_pos null, slot t headed by `fixed_eid` alone.
+__global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restrict__ x, int ldx, int T, int H, int K,
+                                                            const int* __restrict__ dest, const int* __restrict__ lid,
+                                                            const int* __restrict__ pair_pos, int W, int fixed_eid,
+                                                            uint8_t* __restrict__ dst, int stride, int split) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int pieces = H / 256, share = (pieces + split - 1) / split;
+  for (int g = blockIdx.x * warps + (threadIdx.x >> 5); g < T * split; g += gridDim.x * warps) {
+    const int t = g / split, part = g - t * split;
+    // lane d < W: rank d's slot for this token (or -1)
+    long long my_pos = -1;
+    if (pair_pos == nullptr) {
+      if (lane == 0) my_pos = t;
+    } else if (lane < W) {
+      my_pos = pair_pos[(long long)t * W + lane];
+    }
+    const unsigned live = __ballot_sync(0xffffffffu, my_pos >= 0);
+    const bf16* xr = x + (long long)t * ldx;
+    const int c_end = min(H, (part + 1) * share * 256);
+    for (int c0 = part * share * 256; c0 < c_end; c0 += 256) {
+      const int c = c0 + lane * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+      int sfb;
+      const uint2 w = quant8_lanes(u, sfb);
+      const int kb = c / 32;
+      u32 sfw = (u32)sfb << (8 * (kb & 3));
+      sfw |= __shfl_down_sync(0xffffffffu, sfw, 4);
+      sfw |= __shfl_down_sync(0xffffffffu, sfw, 8);
+      for (unsigned m = live; m; m &= m - 1) {
+        const long long pd = __shfl_sync(0xffffffffu, my_pos, __ffs(m) - 1);
+        uint8_t* row = dst + pd * stride;
+        *reinterpret_cast<uint2*>(row + c) = w;
+        if ((lane & 15) == 0) *reinterpret_cast<u32*>(row + H + kb) = sfw;
+      }
+    }
+    if (part == 0 && my_pos >= 0) {  // lane d writes its rank's id list
+      short* ids = reinterpret_cast<short*>(dst + my_pos * stride + H + H / 32);
+      int n = 0;
+      if (pair_pos == nullptr) {
+        ids[n++] = (short)fixed_eid;
+      } else {
+        for (int k = 0; k < K; ++k)
+          if (dest[(long long)t * K + k] == lane) ids[n++] = (short)lid[(long long)t * K + k];
+      }
+      for (; n < K; ++n) ids[n] = -1;
+    }
+  }
+}
+
+// ids[i*KH + j] = the j-th local expert id (int16, -1 none) of per-destination row i
+__global__ void __launch_bounds__(256) ep_ids_k_kernel(const uint8_t* __restrict__ rows, int stride, int R, int H,
+                                                       int KH, int* __restrict__ ids) {
+  const long long n = (long long)R * KH;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const long long i = e / KH;
+    const int j = (int)(e - i * KH);
+    ids[e] = reinterpret_cast<const short*>(rows + i * stride + H + H / 32)[j];
+  }
+}
+
+// Per-destination row i -> permuted rows perm[i*KH + j] (j < KH, -1 skipped) of the tile-major operand and
+// the tiled scales.  One warp a row: each 16-byte piece is read once and written to every destination.
+__global__ void __launch_bounds__(256) ep_unpack_k_kernel(const uint8_t* __restrict__ rows, int stride, int R, int H,
+                                                          int KH, const int* __restrict__ perm,
+                                                          uint8_t* __restrict__ qp, uint8_t* __restrict__ sfp) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int kg4 = H / 128;
+  for (int i = blockIdx.x * warps + (threadIdx.x >> 5); i < R; i += gridDim.x * warps) {
+    const int my_p = lane < KH ? perm[(long long)i * KH + lane] : -1;
+    const unsigned live = __ballot_sync(0xffffffffu, my_p >= 0);
+    if (!live) continue;
+    const uint8_t* row = rows + (long long)i * stride;
+    for (int c0 = 0; c0 < H; c0 += 512) {  // whole warp in step (H may end mid-step): the shuffles need every lane
+      const int c = c0 + lane * 16;
+      const uint4 v = c < H ? *reinterpret_cast<const uint4*>(row + c) : make_uint4(0u, 0u, 0u, 0u);
+      for (unsigned m = live; m; m &= m - 1) {
+        const int p = __shfl_sync(0xffffffffu, my_p, __ffs(m) - 1);
+        if (c < H) *reinterpret_cast<uint4*>(qp + op8_offset(p, c, H)) = v;
+      }
+    }
+    for (int g0 = 0; g0 < H / 128; g0 += 32) {  // whole warp in step: the shuffles below need every lane
+      const int g = g0 + lane;
+      const u32 v = g < H / 128 ? *reinterpret_cast<const u32*>(row + H + 4 * g) : 0u;
+      for (unsigned m = live; m; m &= m - 1) {
+        const int p = __shfl_sync(0xffffffffu, my_p, __ffs(m) - 1);
+        if (g < H / 128) *reinterpret_cast<u32*>(sfp + sf_tiled_offset(p, 4 * g, kg4)) = v;
+      }
+    }
+  }
+}
+
+// The return row of every routed (row, id) pair: pairs numbered in (row, j) order over the valid ids, so
+// out_rows[perm[i*KH + j]] = (valid ids in rows before i) + (valid ids before j in row i).  One block; each
+// thread a contiguous run of rows, a block scan of the runs' counts between two passes.
+__global__ void __launch_bounds__(1024) ep_return_rows_kernel(const int* __restrict__ perm, int R, int KH,
+                                                              int* __restrict__ out_rows) {
+  __shared__ int warp_sum[32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nt = blockDim.x;
+  const int per = (R + nt - 1) / nt, r0 = t * per, r1 = min(R, r0 + per);
+  int cnt = 0;
+  for (int i = r0; i < r1; ++i)
+    for (int j = 0; j < KH; ++j) cnt += perm[(long long)i * KH + j] >= 0;
+  int incl = cnt;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) warp_sum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = lane < (nt >> 5) ? warp_sum[lane] : 0;
+    int wi = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, d);
+      if (lane >= d) wi += y;
+    }
+    if (lane < (nt >> 5)) warp_sum[lane] = wi - v;
+  }
+  __syncthreads();
+  int next = warp_sum[warp] + incl - cnt;
+  for (int i = r0; i < r1; ++i)
+    for (int j = 0; j < KH; ++j) {
+      const int p = perm[(long long)i * KH + j];
+      if (p >= 0) out_rows[p] = next++;
+    }
+}
 
 // `split` warps a source row, each a contiguous share of its 256-column pieces: quantise the row once and
 // write it to each of its destination slots: slot send_pos[t*K + k] with id idx[t*K + k] - dest*E_local

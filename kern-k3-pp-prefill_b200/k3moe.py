@@ -58,6 +58,12 @@ SIGNATURES = {
     "k3moe_ep_ids": (_I, [_P, _I, _I, _I, _P, _P]),
     "k3moe_ep_unpack": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "k3moe_combine_ep": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
+    "k3moe_ep_pair_row_stride": (_I, [_I, _I]),
+    "k3moe_ep_pairs": (_I, [_P, _I, _I, _I, _P, _P]),
+    "k3moe_ep_pack_pairs": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P, _I, _P]),
+    "k3moe_ep_ids_k": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "k3moe_ep_unpack_k": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "k3moe_ep_return_rows": (_I, [_P, _I, _I, _P, _P]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",

@@ -5,21 +5,26 @@ all-to-all (torch.distributed for the plumbing; the only collective of the path)
 Per rank (world W, E_local = E / W experts, T local tokens):
 
 1. router top-k on the local tokens (global expert ids);
-2. a send plan: each pick's destination rank = id // E_local; the routing-table
-   builder with tile 1, run over the expanded (token, k) picks, gives every pick
-   a send slot, grouped by destination and in (token, k) order within one
-   (deterministic), and the per-destination counts;
-3. pack: each token quantised to MXFP8 once and written to its slots as packed
-   rows (E4M3 | UE8M0 | local expert id);
-4. counts all-to-all (the one host synchronisation), then the dispatch
-   all-to-all of packed rows; the local tokens are appended for the shared
-   expert, which every rank holds (local expert E_local);
-5. routing tables over the received rows (K = 1), unpack into the GEMM operand,
-   FC1, FC2 with rows stored back in the order they were received;
-6. the combine all-to-all sends each result row back to its owner, which sums
-   its K rows in k order with f32 FMAs plus the shared row: the single-GPU
-   combine's arithmetic, so the layer's output is bit-identical to one GPU
-   holding every expert.
+2. two plans from the routing-table builder with tile 1 (deterministic): over
+   the expanded (token, k) picks by destination rank, each pick's row among the
+   results that come back (grouped by rank, (token, k) order within one); and
+   over the (token, rank) pairs, each token's slot in the send buffer of every
+   rank holding any of its picks;
+3. pack: each token quantised to MXFP8 once and written once a destination
+   rank, headed by the local expert ids of its picks there (E4M3 | UE8M0 |
+   int16 ids): a token with several experts on one rank crosses the link once;
+4. counts all-to-all (rows and picks a rank; the one host synchronisation),
+   then the dispatch all-to-all of the rows; the local tokens are appended for
+   the shared expert, which every rank holds (local expert E_local);
+5. routing tables over the received rows' ids (K a row), unpack each row into
+   the GEMM operand at all its experts, FC1, FC2 storing each (row, pick)
+   result at its number in (row, pick) order;
+6. the combine all-to-all sends the results back, one row a pick, to the
+   owner, which sums its K rows in k order with f32 FMAs plus the shared row:
+   the single-GPU combine's arithmetic, so the layer's output is bit-identical
+   to one GPU holding every expert.
+
+The fixed-block mode (decode) sends one row a pick in fixed-size blocks.
 
 The reference has no MoE all-to-all (its decode EP replicates the batch and
 all-reduces, roofline/decode.md:164-166); this is the token-sharded layout of
@@ -79,16 +84,62 @@ class GpuOps:
                                                  qp.data_ptr(), sfp.data_ptr(), k3moe._stream()), "ep_unpack")
         return qp, sfp
 
-    def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None):
+    def pair_stride(self, H, K):
+        return k3moe.lib().k3moe_ep_pair_row_stride(H, K)
+
+    def pairs(self, dest, W):
+        T, K = dest.shape
+        out = torch.empty((T, W), dtype=torch.int32, device=dest.device)
+        k3moe._check(k3moe.lib().k3moe_ep_pairs(dest.data_ptr(), T, K, W, out.data_ptr(), k3moe._stream()),
+                     "ep_pairs")
+        return out
+
+    def pack_pairs(self, x, dest, lid, pair_pos, W, n_slots):
+        H, K = x.shape[1], dest.shape[1]
+        st = self.pair_stride(H, K)
+        buf = torch.empty((max(n_slots, 1), st), dtype=torch.uint8, device=x.device)
+        k3moe._check(k3moe.lib().k3moe_ep_pack_pairs(x.data_ptr(), x.stride(0), x.shape[0], H, K, dest.data_ptr(),
+                                                     lid.data_ptr(), pair_pos.data_ptr(), W, 0, buf.data_ptr(), st,
+                                                     k3moe._stream()), "ep_pack_pairs")
+        return buf
+
+    def pack_pair_rows(self, x, K, eid, dst):
+        H = x.shape[1]
+        k3moe._check(k3moe.lib().k3moe_ep_pack_pairs(x.data_ptr(), x.stride(0), x.shape[0], H, K, None, None, None, 1,
+                                                     eid, dst.data_ptr(), dst.shape[1], k3moe._stream()),
+                     "ep_pack_pair_rows")
+
+    def ids_k(self, rows, R, H, K):
+        ids = torch.empty((R, K), dtype=torch.int32, device=rows.device)
+        k3moe._check(k3moe.lib().k3moe_ep_ids_k(rows.data_ptr(), rows.shape[1], R, H, K, ids.data_ptr(),
+                                                k3moe._stream()), "ep_ids_k")
+        return ids
+
+    def unpack_k(self, rows, R, H, K, tb):
+        qp = torch.empty((tb.cap_rows, H), dtype=torch.uint8, device=rows.device)
+        sfp = torch.empty(tb.cap_rows * H // 32, dtype=torch.uint8, device=rows.device)
+        k3moe._check(k3moe.lib().k3moe_ep_unpack_k(rows.data_ptr(), rows.shape[1], R, H, K, tb.exp2perm.data_ptr(),
+                                                   qp.data_ptr(), sfp.data_ptr(), k3moe._stream()), "ep_unpack_k")
+        return qp, sfp
+
+    def return_rows(self, tb, R, K):
+        out = torch.empty(tb.cap_rows, dtype=torch.int32, device=tb.exp2perm.device)
+        k3moe._check(k3moe.lib().k3moe_ep_return_rows(tb.exp2perm.data_ptr(), R, K, out.data_ptr(),
+                                                      k3moe._stream()), "ep_return_rows")
+        return out
+
+    def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None, out_rows=None):
+        """FC1 and FC2; FC2 stores permuted row r at row out_rows[r] (default: tb.route_map, the received row)."""
         if events:
             events["fc1"][0].record()
         f1q, f1sf = k3moe.fc1(w["w13"], w["w13_sf"], qp, sfp, tb, H, I, n_experts, self.err)
         if events:
             events["fc1"][1].record()
-        y = torch.empty((n_rows, H), dtype=torch.bfloat16, device=qp.device)
+        rows = tb.route_map if out_rows is None else out_rows
+        y = torch.empty((max(n_rows, 1), H), dtype=torch.bfloat16, device=qp.device)
         k3moe._check(k3moe.lib().k3moe_fc2_to_rows(
             w["w2"].data_ptr(), w["w2_sf"].data_ptr(), f1q.data_ptr(), f1sf.data_ptr(), tb.cta_batch.data_ptr(),
-            tb.cta_limit.data_ptr(), tb.meta.data_ptr(), tb.route_map.data_ptr(), y.data_ptr(), H, I, n_experts,
+            tb.cta_limit.data_ptr(), tb.meta.data_ptr(), rows.data_ptr(), y.data_ptr(), H, I, n_experts,
             tb.cap_rows, tb.max_ctas, self.err.data_ptr(), k3moe._stream()), "fc2_to_rows")
         return y
 
@@ -215,39 +266,48 @@ class EPMoELayer:
         T = x.shape[0]
         idx, wts = ops.topk(S, self.bias, self.rs, K)
         dest, lid = self._route(idx)
-        # one pick a "row": several picks of a token may go to the same rank, and the table builder
-        # ranks rows, so the plan runs over the expanded (token, k) sequence
+        # the picks' plan: every pick's row in the returned results (grouped by rank, (token, k) order within
+        # one) for the combine, and the picks a rank gets
         plan = ops.tables(dest.reshape(-1, 1).contiguous(), W, 1)
-        send_pos = plan.exp2perm.reshape(T, K)          # [T, K] slot of each pick
-        send_counts = plan.counts[:W].to(torch.int64)   # picks to each rank
-        send = ops.pack(x, lid.contiguous(), send_pos, LOCAL_IDS, T * K)
-        recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, [1] * W, [1] * W)
-        sc = send_counts.tolist()
+        send_pos = plan.exp2perm.reshape(T, K)          # [T, K] return row of each pick
+        pick_counts = plan.counts[:W].to(torch.int64)
+        # the rows' plan: a token travels once to each rank holding any of its picks (token order within a rank)
+        pairs = ops.pairs(dest.contiguous(), W)
+        rplan = ops.tables(pairs, W, 1)
+        row_counts = rplan.counts[:W].to(torch.int64)
+        send = ops.pack_pairs(x, dest.contiguous(), lid.contiguous(), rplan.exp2perm.reshape(T, W), W,
+                              T * min(W, K))
+        counts = torch.stack([row_counts, pick_counts], 1).contiguous()  # [W, 2]: rows, picks to each rank
+        recv_counts = torch.empty_like(counts)
+        self._a2a(recv_counts, counts, [1] * W, [1] * W)
+        sc_rows, sc_picks = (counts[:, 0].tolist(), counts[:, 1].tolist())
         rc = recv_counts.tolist()
-        R_recv = sum(rc)
-        R_all = R_recv + (T if self.shared else 0)
+        rc_rows, rc_picks = [r[0] for r in rc], [r[1] for r in rc]
+        R_recv, P_recv = sum(rc_rows), sum(rc_picks)
+        R_all, P_all = R_recv + (T if self.shared else 0), P_recv + (T if self.shared else 0)
         stride = send.shape[1]
         recv = torch.empty((max(R_all, 1), stride), dtype=torch.uint8, device=send.device)
         if events:
             events["dispatch"][0].record()
-        self._a2a(recv[:R_recv], send, rc, sc)
+        self._a2a(recv[:R_recv], send[:sum(sc_rows)], rc_rows, sc_rows)
         if events:
             events["dispatch"][1].record()
         if self.shared:
-            ops.pack_rows(x, El, recv[R_recv:R_all])
-        ids = ops.ids(recv, R_all, H)
+            ops.pack_pair_rows(x, K, El, recv[R_recv:R_all])
+        ids = ops.ids_k(recv, R_all, H, K)               # [R_all, K] local ids of each row's picks
         tb = ops.tables(ids, El + self.shared, 128)
-        qp, sfp = ops.unpack(recv, R_all, H, tb)
-        y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, R_all, events)
+        qp, sfp = ops.unpack_k(recv, R_all, H, K, tb)
+        out_rows = ops.return_rows(tb, R_all, K)         # results in (row, pick) order: returned picks, shared
+        y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, P_all, events, out_rows=out_rows)
         back = torch.empty((T * K, H), dtype=y.dtype, device=y.device)
         if events:
             events["combine"][0].record()
-        self._a2a(back, y[:R_recv], sc, rc)
+        self._a2a(back, y[:P_recv], sc_picks, rc_picks)
         if events:
             events["combine"][1].record()
-        self.last = {"received_rows": R_recv, "sent_rows": T * K, "tables": tb}
-        shared_rows = y[R_recv:R_all] if self.shared else None
+        self.last = {"received_rows": R_recv, "received_picks": P_recv, "sent_rows": sum(sc_rows),
+                     "sent_picks": T * K, "tables": tb}
+        shared_rows = y[P_recv:P_all] if self.shared else None
         return ops.combine(back, send_pos, wts, shared_rows, T, K, H)
 
 

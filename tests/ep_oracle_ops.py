@@ -85,13 +85,83 @@ class OracleOps:
             sfp[((p // 128) * kg4 + kb // 4) * 512 + (p % 32) * 16 + ((p % 128) // 32) * 4 + kb % 4] = r[i, H:H + H // 32]
         return qp.reshape(tb.cap_rows, H), sfp
 
-    def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None):
+    @staticmethod
+    def pair_stride(H, K):
+        return (H + H // 32 + 2 * K + 15) // 16 * 16
+
+    def pairs(self, dest, W):
+        d = _np(dest)
+        out = np.full((d.shape[0], W), -1, np.int32)
+        for t in range(d.shape[0]):
+            for r in set(d[t].tolist()):
+                out[t, r] = r
+        return torch.from_numpy(out)
+
+    def _pair_row(self, buf, p, q, sf, ids, K):
+        H = q.shape[0]
+        buf[p, :H] = q
+        buf[p, H:H + H // 32] = sf
+        hdr = np.full(K, -1, np.int16)
+        hdr[:len(ids)] = ids
+        buf[p, H + H // 32:H + H // 32 + 2 * K] = hdr.view(np.uint8)
+
+    def pack_pairs(self, x, dest, lid, pair_pos, W, n_slots):
+        H, K = x.shape[1], dest.shape[1]
+        q, sf = self._rows(x)
+        buf = np.zeros((max(n_slots, 1), self.pair_stride(H, K)), np.uint8)
+        d, l, pp = _np(dest), _np(lid), _np(pair_pos)
+        for t in range(d.shape[0]):
+            for r in range(W):
+                if pp[t, r] >= 0:
+                    self._pair_row(buf, pp[t, r], q[t], sf[t], [l[t, k] for k in range(K) if d[t, k] == r], K)
+        return torch.from_numpy(buf)
+
+    def pack_pair_rows(self, x, K, eid, dst):
+        q, sf = self._rows(x)
+        d = _np(dst)
+        for t in range(q.shape[0]):
+            self._pair_row(d, t, q[t], sf[t], [eid], K)
+
+    def ids_k(self, rows, R, H, K):
+        r = _np(rows)[:R, H + H // 32:H + H // 32 + 2 * K].copy()
+        return torch.from_numpy(r.view(np.int16).astype(np.int32).reshape(R, K))
+
+    def unpack_k(self, rows, R, H, K, tb):
+        r = _np(rows)
+        perm = _np(tb.exp2perm).reshape(R, K)
+        qp = np.zeros(tb.cap_rows * H, np.uint8)
+        sfp = np.zeros(tb.cap_rows * H // 32, np.uint8)
+        kg4 = H // 128
+        k = np.arange(H)
+        kb = np.arange(H // 32)
+        for i in range(R):
+            for j in range(K):
+                p = int(perm[i, j])
+                if p < 0:
+                    continue
+                qp[((p // 128) * (H // 128) + k // 128) * 16384 + (p % 128) * 128 + k % 128] = r[i, :H]
+                sfp[((p // 128) * kg4 + kb // 4) * 512 + (p % 32) * 16 + ((p % 128) // 32) * 4 + kb % 4] = \
+                    r[i, H:H + H // 32]
+        return qp.reshape(tb.cap_rows, H), sfp
+
+    def return_rows(self, tb, R, K):
+        perm = _np(tb.exp2perm).reshape(R, K)
+        out = np.full(tb.cap_rows, -1, np.int32)
+        n = 0
+        for i in range(R):
+            for j in range(K):
+                if perm[i, j] >= 0:
+                    out[perm[i, j]] = n
+                    n += 1
+        return torch.from_numpy(out)
+
+    def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None, out_rows=None):
         nne = int(tb.meta[0])
         wn = {k: _np(v) for k, v in w.items()}
         f1q, f1sf = oracle.fc1(wn["w13"], wn["w13_sf"], qp, sfp, tb.cta_batch, tb.cta_limit, 0, nne, H, I)
         yp = oracle.fc2(wn["w2"], wn["w2_sf"], f1q, f1sf, tb.cta_batch, tb.cta_limit, 0, nne, H, I)
-        y = np.zeros((n_rows, H), np.uint16)
-        rmap = _np(tb.route_map)
+        y = np.zeros((max(n_rows, 1), H), np.uint16)
+        rmap = _np(tb.route_map if out_rows is None else out_rows)
         for c in range(nne):
             for r in range(c * 128, int(tb.cta_limit[c])):
                 y[rmap[r]] = yp[r]

@@ -22,6 +22,12 @@ def _free_port():
 
 
 CFG = dict(T=96, H=256, I=256, E=8, K=2, shared=1, rs=2.5, seed=11)
+# several picks of a token on one rank (4 of 8 experts a rank, top-4): one dispatched row carries them all
+CFG_DENSE = dict(T=64, H=256, I=256, E=8, K=4, shared=1, rs=2.5, seed=12)
+
+
+def _cfg(mode):
+    return CFG_DENSE if mode == "dense" else CFG
 
 
 def _worker(rank, world, port, outdir, mode):
@@ -39,7 +45,7 @@ def _worker(rank, world, port, outdir, mode):
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=__import__("datetime").timedelta(seconds=60))
-    c = C.make_case(**CFG)
+    c = C.make_case(**_cfg(mode))
     T_l = c.T // world
     rows = slice(rank * T_l, (rank + 1) * T_l)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
@@ -55,10 +61,12 @@ def _worker(rank, world, port, outdir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "fixed", "placed"])
+@pytest.mark.parametrize("mode", ["counts", "dense", "fixed", "placed"])
 def test_ep2_gloo_matches_single_device(mode):
-    # fixed: the fixed-block all-to-all (no counts exchange, empty slots marked -1) of decode-sized batches;
-    # placed: experts dealt to the ranks by router bias (balanced_owner) instead of in contiguous blocks
+    # counts / dense: one dispatched row a (token, rank) pair, headed by the token's picks there (dense: top-4
+    # of 8 experts, so most rows carry several); fixed: the fixed-block all-to-all (no counts exchange, empty
+    # slots marked -1) of decode-sized batches; placed: experts dealt to the ranks by router bias
+    # (balanced_owner) instead of in contiguous blocks
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
@@ -71,6 +79,6 @@ def test_ep2_gloo_matches_single_device(mode):
                 p.kill()
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         got = np.concatenate([np.load(os.path.join(d, f"out{r}.npy")) for r in range(2)])
-    c = cases.make_case(**CFG)
+    c = cases.make_case(**_cfg(mode))
     ref, _ = cases.oracle_forward(c)
     assert np.array_equal(got, ref)
