@@ -85,3 +85,52 @@ def test_unpack_ffn_combine(setup):
     out_g = gops.combine(back, send_pos, wts, y_g[r0:R], c.T, K, H)
     out_o = oops.combine(back.cpu(), send_pos.cpu(), wts.cpu(), y_g[r0:R].cpu(), c.T, K, H)
     assert torch.equal(out_g.cpu().view(torch.int16), out_o.view(torch.int16))
+
+
+def test_pair_rows_plan_pack_unpack_return(setup):
+    """The per-destination dispatch on one GPU against the oracle ops: the (token, rank) pairs and their plan,
+    the packed rows with their id headers, the received ids (K a row), the unpacked operand at every expert
+    of a row, and the return-row map FC2 stores by."""
+    c, g, gops, oops = setup
+    idx, _ = gops.topk(g["S"], g["bias"], g["rs"], K)
+    dest = (idx // El).to(torch.int32).contiguous()
+    lid = (idx - dest * El).to(torch.int32).contiguous()
+    pairs_g = gops.pairs(dest, W)
+    pairs_o = oops.pairs(dest.cpu(), W)
+    assert np.array_equal(_np(pairs_g), _np(pairs_o))
+    rplan = gops.tables(pairs_g, W, 1)
+    n_pairs = int(rplan.counts[:W].sum())
+    assert n_pairs < c.T * K  # several picks of a token share a rank
+    pp = rplan.exp2perm.reshape(c.T, W)
+    sg = gops.pack_pairs(g["x"], dest, lid, pp, W, c.T * min(W, K))
+    so = oops.pack_pairs(g["x"].cpu(), dest.cpu(), lid.cpu(), pp.cpu(), W, c.T * min(W, K))
+    used = H + H // 32 + 2 * K
+    assert np.array_equal(_np(sg)[:n_pairs, :used], _np(so)[:n_pairs, :used])
+    # received: rank 0's rows, then the shared expert's local rows
+    r0 = int(rplan.counts[0])
+    R = r0 + c.T
+    recv = torch.empty((R, sg.shape[1]), dtype=torch.uint8, device=sg.device)
+    recv[:r0] = sg[:r0]
+    gops.pack_pair_rows(g["x"], K, El, recv[r0:R])
+    recv_o = recv.cpu().clone()
+    oops.pack_pair_rows(g["x"].cpu(), K, El, recv_o[r0:R])
+    assert np.array_equal(_np(recv)[:, :used], _np(recv_o)[:, :used])
+    ids = gops.ids_k(recv, R, H, K)
+    assert np.array_equal(_np(ids), _np(oops.ids_k(recv_o, R, H, K)))
+    assert int((ids >= 0).sum()) == int((dest == 0).sum()) + c.T  # every pick bound for rank 0, and the shared
+    tb_g = gops.tables(ids, El + SH, 128)
+    tb_o = oops.tables(ids.cpu(), El + SH, 128)
+    assert np.array_equal(_np(tb_g.exp2perm), _np(tb_o.exp2perm))
+    qp_g, sfp_g = gops.unpack_k(recv, R, H, K, tb_g)
+    qp_o, sfp_o = oops.unpack_k(recv_o, R, H, K, tb_o)
+    rows = np.unique(_np(tb_g.exp2perm).reshape(-1))
+    rows = rows[rows >= 0]
+    assert np.array_equal(oracle.t128_rows(_np(qp_g), rows, H), oracle.t128_rows(qp_o, rows, H))
+    r = rows[:, None].astype(np.int64)
+    kb = np.arange(H // 32)[None, :]
+    off = ((r // 128) * (H // 128) + kb // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + kb % 4
+    assert np.array_equal(_np(sfp_g)[off], sfp_o[off])
+    ret_g = _np(gops.return_rows(tb_g, R, K))
+    ret_o = _np(oops.return_rows(tb_o, R, K))
+    assert np.array_equal(ret_g[rows], ret_o[rows])
+    assert np.array_equal(np.sort(ret_g[rows]), np.arange(rows.size))
