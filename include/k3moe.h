@@ -157,9 +157,10 @@ int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc
                       k3moe_stream_t stream);
 
 /* ---------------------------------------------------------------- expert parallelism
- * Tokens are owned by their rank; experts are split in contiguous blocks of
- * E_local.  A routed pick travels as one packed row (dispatch wire format) of
- * k3moe_ep_row_stride(H) bytes: E4M3 [H] | UE8M0 [H/32] | int32 local expert id.
+ * Tokens are owned by their rank; each rank holds E_local experts.  Two wire
+ * formats: one row a pick (the fixed-block decode mode), k3moe_ep_row_stride(H)
+ * bytes: E4M3 [H] | UE8M0 [H/32] | int32 local expert id; and one row a token
+ * and destination rank (below, k3moe_ep_pack_pairs).
  * No counterpart in the reference for the MoE (its decode EP replicates the
  * batch and all-reduces: roofline/decode.md:164-166; k3_ar_fused.cu:916). */
 int k3moe_ep_row_stride(int H);
