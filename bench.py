@@ -351,7 +351,8 @@ def run_ep(args, world, rank, dev):
     x, S, bias, rs = rank_inputs(T, E, rank, dev)
     owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
     w = rank_weights(E, mine, dev)
-    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, owner=owner)
+    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, owner=owner,
+                                overlap_chunks=args.ep_overlap, fc2_grid_cap=args.ep_fc2_cap)
     for _ in range(args.warmup):
         layer.forward(S, x)
     torch.cuda.synchronize()
@@ -398,7 +399,8 @@ def run_ep(args, world, rank, dev):
             "config": {"workload": f"K3-shape prefill MoE layer, expert parallel over {world} GPUs (config 4 layout)",
                        "T_per_gpu": T, "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I,
                        "rs": RS, "global_batch": T * world, "seq_len": T, "parallelism": f"ep{world}",
-                       "expert_placement": args.ep_placement,
+                       "expert_placement": args.ep_placement, "fc2_slices": args.ep_overlap,
+                       "fc2_grid_cap": args.ep_fc2_cap,
                        "l2": "inputs larger than L2: each GPU streams its experts' weights every step"},
             "tflops": flops / (ms / 1e3) / 1e12,
             "a2a_ms": {"dispatch": disp_ms, "combine": comb_ms},
@@ -410,7 +412,9 @@ def run_ep(args, world, rank, dev):
                     "d2h_bytes_per_step": int(x.numel() * 2) * world,
                     "copies": "every step's x, S in and output back over PCIe, on side streams overlapping the "
                               "neighbouring steps' compute (double buffers)"},
-            "gpu_launches": 14 * args.steps,
+            # topk, 2 x 3 plan launches, pairs, pack, shared pack, ids, 3 table launches, unpack, return rows,
+            # FC1, FC2 (a launch a slice), combine
+            "gpu_launches": (18 + args.ep_overlap) * args.steps,
             "clocks": clk.summary(),
             "cpu_baseline": None,
         }
@@ -643,6 +647,10 @@ def main():
                     help="N > 1: experts dealt to ranks by router bias (balanced) or in contiguous blocks")
     ap.add_argument("--zipf", action="store_true",
                     help="config 3: the routing bias makes expert popularity Zipf(1.1) (N = 1 prefill)")
+    ap.add_argument("--ep-overlap", type=int, default=1,
+                    help="N > 1: FC2 in this many column slices, each returned by its own all-to-all beside the next")
+    ap.add_argument("--ep-fc2-cap", type=int, default=0,
+                    help="N > 1 with --ep-overlap > 1: FC2's persistent blocks (0: one an SM), SMs left to NCCL")
     ap.add_argument("--native", action="store_true",
                     help="the layer at the reference's own K3 shapes (latent 3584, I 3072, top-16, SiTU), N = 1")
     args = ap.parse_args()

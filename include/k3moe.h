@@ -149,6 +149,14 @@ int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_pe
                   uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
                   int activation, k3moe_stream_t stream);
 
+/* FC2 over the output columns [col0, col0 + ncols) only (multiples of 256), stored at
+ * out_bf16 + out_rows[r] * ldo (out_rows null: row r), with at most grid_cap persistent
+ * blocks (0: one an SM; fewer leave SMs to a collective running beside it). */
+int k3moe_fc2_cols(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+                   const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const int32_t* out_rows,
+                   void* out_bf16, int ldo, int col0, int ncols, int H, int I, int n_experts, int cap_rows,
+                   int max_ctas, int grid_cap, uint32_t* err, k3moe_stream_t stream);
+
 /* FC2 storing permuted row r at row out_rows[r] of fc2_bf16 (the expert-parallel
  * layer passes route_map, so rows come out in the order they were received). */
 int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
@@ -199,6 +207,14 @@ int k3moe_ep_return_rows(const int32_t* perm, int R, int K, int32_t* out_rows, k
  * the combine over rows returned by the combine all-to-all (shared_bf16 may be null). */
 int k3moe_combine_ep(const void* back_bf16, const int32_t* pos, const float* wts, const void* shared_bf16,
                      int ld_shared, void* out_bf16, int ldo, int T, int K, int cols, k3moe_stream_t stream);
+
+/* k3moe_combine_ep over rows that come as column chunks of chunk_cols columns (cols a multiple of it):
+ * chunk j of returned row p at back + j * back_chunk_stride + p * back_ld elements, of shared row t at
+ * shared + j * shared_chunk_stride + t * ld_shared (the expert-parallel layer returns FC2's results one
+ * column chunk at a time, each all-to-all overlapping the next chunk's FC2). */
+int k3moe_combine_ep_chunked(const void* back_bf16, long long back_chunk_stride, int back_ld, const int32_t* pos,
+                             const float* wts, const void* shared_bf16, long long shared_chunk_stride, int ld_shared,
+                             void* out_bf16, int ldo, int T, int K, int cols, int chunk_cols, k3moe_stream_t stream);
 
 /* ---------------------------------------------------------------- combine
  * out[t] = bf16( sum over k = 0..K-1 with exp2perm >= 0 of fma(wts, fc2[p], acc)

@@ -97,11 +97,21 @@ void launch_topk(const float* S, int lds, const float* bias, const bf16* rs, int
   topk_kernel<EPL><<<(unsigned)blocks, warps * 32, 0, s>>>(S, lds, bias, rs, T, E, K, idx, wts);
 }
 
+// FC2 may compute a column slice [col0, col0 + ncols) of its output into a buffer of row stride ldo (ncols 0:
+// all H columns, row stride H), with at most grid_cap persistent blocks (0: one an SM).
 int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* act, const uint8_t* act_sf,
                 const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* out_q,
                 uint8_t* out_sf, void* out_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas,
-                uint32_t* err, cudaStream_t stream, const int32_t* out_rows = nullptr, int activation = 0) {
+                uint32_t* err, cudaStream_t stream, const int32_t* out_rows = nullptr, int activation = 0,
+                int col0 = 0, int ncols = 0, int ldo = 0, int grid_cap = 0) {
   if (activation != 0 && activation != 1) return K3MOE_EINVAL;
+  if (ncols == 0) {
+    ncols = H;
+    ldo = H;
+  }
+  if (col0 < 0 || col0 % gemm::BN || ncols <= 0 || ncols % gemm::BN || col0 + ncols > H || ldo < ncols || ldo % 16 ||
+      grid_cap < 0)
+    return K3MOE_EINVAL;
   if (H <= 0 || I <= 0 || H % 256 || I % 256 || n_experts <= 0 || cap_rows <= 0 || cap_rows % 128 || max_ctas <= 0 ||
       (long long)max_ctas * 128 > cap_rows)
     return K3MOE_EINVAL;
@@ -130,13 +140,15 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   p.K = K;
   p.rows_per_expert = rows_per_expert;
   p.n_experts = n_experts;
-  p.nfb = mode == MODE_FC1 ? I / 128 : H / gemm::BN;  // FC1: 128 features (gate + up rows), FC2: 256 outputs
-  p.out_cols = mode == MODE_FC1 ? I : H;
+  p.nfb = mode == MODE_FC1 ? I / 128 : ncols / gemm::BN;  // FC1: 128 features (gate + up rows), FC2: 256 outputs
+  p.fb0 = mode == MODE_FC1 ? 0 : col0 / gemm::BN;
+  p.out_cols = mode == MODE_FC1 ? I : ldo;
   p.cap_rows = cap_rows;
   p.max_ctas = max_ctas;
   p.trace = g_trace;
   const long long max_units = (long long)max_ctas * p.nfb;
-  const int grid = (int)std::min<long long>(num_sms(current_device()), max_units);
+  const int sms = num_sms(current_device());
+  const int grid = (int)std::min<long long>(grid_cap > 0 ? std::min(grid_cap, sms) : sms, max_units);
   if (mode == MODE_FC1) {
     if (!set_smem_once(grouped_gemm_kernel<MODE_FC1>, gemm::SMEM_BYTES, 0)) return K3MOE_ELAUNCH;
     grouped_gemm_kernel<MODE_FC1><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
@@ -388,6 +400,16 @@ int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc
                      n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream), out_rows);
 }
 
+int k3moe_fc2_cols(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+                   const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const int32_t* out_rows,
+                   void* out_bf16, int ldo, int col0, int ncols, int H, int I, int n_experts, int cap_rows,
+                   int max_ctas, int grid_cap, uint32_t* err, k3moe_stream_t stream) {
+  if (ncols <= 0) return K3MOE_EINVAL;
+  return gemm_launch(MODE_FC2, w2, w2_sf, fc1_q, fc1_sf, cta_batch, cta_limit, meta, nullptr, nullptr, out_bf16, H, I,
+                     n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream), out_rows, 0, col0,
+                     ncols, ldo, grid_cap);
+}
+
 int k3moe_ep_row_stride(int H) { return H > 0 && H % 256 == 0 ? (H + H / 32 + 4 + 15) / 16 * 16 : 0; }
 
 int k3moe_ep_pack(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* idx, const int32_t* send_pos,
@@ -484,7 +506,22 @@ int k3moe_combine_ep(const void* back_bf16, const int32_t* pos, const float* wts
   if (T == 0) return K3MOE_OK;
   combine_ep_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const bf16*>(back_bf16), pos, wts, reinterpret_cast<const bf16*>(shared_bf16), ld_shared,
-      reinterpret_cast<bf16*>(out_bf16), ldo, T, K, cols);
+      reinterpret_cast<bf16*>(out_bf16), ldo, T, K, cols, cols, 0, cols, 0);
+  return launch_status();
+}
+
+int k3moe_combine_ep_chunked(const void* back_bf16, long long back_chunk_stride, int back_ld, const int32_t* pos,
+                             const float* wts, const void* shared_bf16, long long shared_chunk_stride, int ld_shared,
+                             void* out_bf16, int ldo, int T, int K, int cols, int chunk_cols, k3moe_stream_t stream) {
+  if (T < 0 || K < 1 || K > 16 || cols <= 0 || cols % 8 || ldo < cols || ldo % 8 || chunk_cols <= 0 ||
+      chunk_cols % 8 || cols % chunk_cols || back_ld < chunk_cols || back_ld % 8 || back_chunk_stride % 8 ||
+      (shared_bf16 && (ld_shared < chunk_cols || ld_shared % 8 || shared_chunk_stride % 8)))
+    return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  combine_ep_kernel<<<T, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(back_bf16), pos, wts, reinterpret_cast<const bf16*>(shared_bf16), ld_shared,
+      reinterpret_cast<bf16*>(out_bf16), ldo, T, K, cols, chunk_cols, back_chunk_stride, back_ld,
+      shared_chunk_stride);
   return launch_status();
 }
 

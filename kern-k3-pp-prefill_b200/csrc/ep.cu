@@ -246,11 +246,15 @@ __global__ void __launch_bounds__(256) ep_unpack_kernel(const uint8_t* __restric
 }
 
 // out[t] = bf16( sum_{k, pos>=0} fma(w[t,k], back[pos[t,k]], acc) (+ shared[t]) ), f32, k in order:
-// the single-GPU combine's arithmetic, over rows returned by the combine all-to-all.
+// the single-GPU combine's arithmetic, over rows returned by the combine all-to-all.  The returned rows (and
+// the shared rows) may come as column chunks of chunk_cols columns: chunk j of row p at
+// back + j * back_cs + p * back_ld (shared: shared_rows + j * shared_cs + t * ld_shared).
 __global__ void __launch_bounds__(256) combine_ep_kernel(const bf16* __restrict__ back, const int* __restrict__ pos,
                                                          const float* __restrict__ wts,
                                                          const bf16* __restrict__ shared_rows, int ld_shared,
-                                                         bf16* __restrict__ out, int ldo, int T, int K, int cols) {
+                                                         bf16* __restrict__ out, int ldo, int T, int K, int cols,
+                                                         int chunk_cols, long long back_cs, int back_ld,
+                                                         long long shared_cs) {
   __shared__ int sp[16];
   __shared__ float sw[16];
   const int t = blockIdx.x;
@@ -260,12 +264,14 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(const bf16* __restrict_
   }
   __syncthreads();
   for (int h = threadIdx.x; h < cols / 8; h += blockDim.x) {
+    const int ch = (8 * h) / chunk_cols, within = 8 * h - ch * chunk_cols;
+    const bf16* bk = back + ch * back_cs + within;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < K; ++k) {
       const int p = sp[k];
       if (p < 0) continue;
       const float w = sw[k];
-      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(back + (long long)p * cols) + h);
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(bk + (long long)p * back_ld));
       const u32* pv = reinterpret_cast<const u32*>(&u);
 #pragma unroll
       for (int l = 0; l < 4; ++l) {
@@ -275,7 +281,7 @@ __global__ void __launch_bounds__(256) combine_ep_kernel(const bf16* __restrict_
       }
     }
     if (shared_rows) {
-      const uint4 u = *(reinterpret_cast<const uint4*>(shared_rows + (long long)t * ld_shared) + h);
+      const uint4 u = *reinterpret_cast<const uint4*>(shared_rows + ch * shared_cs + (long long)t * ld_shared + within);
       const u32* pv = reinterpret_cast<const u32*>(&u);
 #pragma unroll
       for (int l = 0; l < 4; ++l) {

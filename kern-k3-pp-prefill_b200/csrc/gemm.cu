@@ -85,6 +85,7 @@ struct GemmParams {
   int max_ctas;             // capacity of the CTA tables
   unsigned long long* trace;  // optional per-role cycle counters (16 a mode), or null
   int act;                  // FC1 gate: 0 SwiGLU silu(g)*u, 1 K3's SiTU 4 tanh(g/4) sigmoid(g) * 25 tanh(u/25)
+  int fb0;                  // FC2: the first 256-column block computed (a column slice [256 fb0, 256 (fb0 + nfb)))
 };
 
 // FC1's gated activation of (gate g, up u)
@@ -115,7 +116,7 @@ __device__ __forceinline__ Unit decode_unit(const GemmParams& p, int u) {
 template <int MODE>
 __device__ __forceinline__ int weight_row(const GemmParams& p, const Unit& w, int h) {
   if (MODE == MODE_FC1) return w.e * p.rows_per_expert + h * (p.rows_per_expert / 2) + w.fb * 128;
-  return w.e * p.rows_per_expert + w.fb * gemm::BN + h * 128;
+  return w.e * p.rows_per_expert + (p.fb0 + w.fb) * gemm::BN + h * 128;
 }
 
 template <int MODE>

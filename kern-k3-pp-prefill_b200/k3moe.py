@@ -59,6 +59,8 @@ SIGNATURES = {
     "k3moe_ep_unpack": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "k3moe_combine_ep": (_I, [_P, _P, _P, _P, _I, _P, _I, _I, _I, _I, _P]),
     "k3moe_ep_pair_row_stride": (_I, [_I, _I]),
+    "k3moe_fc2_cols": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "k3moe_combine_ep_chunked": (_I, [_P, _L, _I, _P, _P, _P, _L, _I, _P, _I, _I, _I, _I, _I, _P]),
     "k3moe_ep_pairs": (_I, [_P, _I, _I, _I, _P, _P]),
     "k3moe_ep_pack_pairs": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P, _I, _P]),
     "k3moe_ep_ids_k": (_I, [_P, _I, _I, _I, _I, _P, _P]),

@@ -128,6 +128,47 @@ class GpuOps:
                                                       k3moe._stream()), "ep_return_rows")
         return out
 
+    def fc1(self, w, qp, sfp, tb, H, I, n_experts):
+        return k3moe.fc1(w["w13"], w["w13_sf"], qp, sfp, tb, H, I, n_experts, self.err)
+
+    def fc2_cols(self, w, f1q, f1sf, tb, H, I, n_experts, out_rows, out, col0, ncols, grid_cap=0):
+        """FC2's output columns [col0, col0 + ncols) into `out` (row stride out.stride(0)), row out_rows[r]."""
+        k3moe._check(k3moe.lib().k3moe_fc2_cols(
+            w["w2"].data_ptr(), w["w2_sf"].data_ptr(), f1q.data_ptr(), f1sf.data_ptr(), tb.cta_batch.data_ptr(),
+            tb.cta_limit.data_ptr(), tb.meta.data_ptr(), out_rows.data_ptr(), out.data_ptr(), out.stride(0), col0,
+            ncols, H, I, n_experts, tb.cap_rows, tb.max_ctas, grid_cap, self.err.data_ptr(), k3moe._stream()),
+            "fc2_cols")
+
+    def side_stream(self):
+        return torch.cuda.Stream(device=self.device)
+
+    def after(self, side):
+        """`side` waits for the work queued on the current stream so far."""
+        side.wait_stream(torch.cuda.current_stream())
+
+    def on(self, side):
+        return torch.cuda.stream(side)
+
+    def join(self, side, *tensors):
+        """The current stream waits for `side`; `tensors` were used on it."""
+        torch.cuda.current_stream().wait_stream(side)
+        for t in tensors:
+            t.record_stream(side)
+
+    def combine_chunked(self, back, send_pos, wts, shared_rows, T, K, H):
+        """combine() over results that came back as column chunks: back [C, rows, H/C], shared_rows [C, T, H/C]
+        (a view) or None."""
+        C, cc = back.shape[0], back.shape[2]
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=back.device)
+        sp = shared_rows.data_ptr() if shared_rows is not None else None
+        scs = shared_rows.stride(0) if shared_rows is not None else 0
+        sld = shared_rows.stride(1) if shared_rows is not None else 0
+        k3moe._check(k3moe.lib().k3moe_combine_ep_chunked(back.data_ptr(), back.stride(0), back.stride(1),
+                                                          send_pos.data_ptr(), wts.data_ptr(), sp, scs, sld,
+                                                          out.data_ptr(), H, T, K, H, cc, k3moe._stream()),
+                     "combine_ep_chunked")
+        return out
+
     def ffn(self, w, qp, sfp, tb, H, I, n_experts, n_rows, events=None, out_rows=None):
         """FC1 and FC2; FC2 stores permuted row r at row out_rows[r] (default: tb.route_map, the received row)."""
         if events:
@@ -175,12 +216,15 @@ class EPMoELayer:
     """
 
     def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None, fixed_tokens=None,
-                 owner=None):
+                 owner=None, overlap_chunks=1, fc2_grid_cap=0):
         """fixed_tokens: when set (at most that many tokens a call), every rank sends fixed-size blocks of
         fixed_tokens*K slots to every rank, empty slots marked by local expert id -1: no host
         synchronisation, so a whole step can be captured in a CUDA graph (decode-sized batches).
         owner: int [E], the rank holding each expert (E / world each; a rank's experts in increasing id order
-        are its local experts 0, 1, ...; `w` holds them in that order).  None: contiguous blocks."""
+        are its local experts 0, 1, ...; `w` holds them in that order).  None: contiguous blocks.
+        overlap_chunks: C > 1 splits FC2 into C column slices (H / C a multiple of 256) and returns each slice's
+        results with its own all-to-all on a side stream while the next slice computes; fc2_grid_cap then
+        bounds FC2's persistent blocks (0: one an SM) to leave SMs to the collective."""
         self.fixed_tokens = fixed_tokens
         self.group = group
         self.rank = dist.get_rank(group)
@@ -201,7 +245,11 @@ class EPMoELayer:
                 local[mine] = torch.arange(mine.numel())
             dev = bias.device
             self.owner_map = (owner.to(torch.int32).to(dev), local.to(torch.int32).to(dev))
+        if overlap_chunks < 1 or H % (256 * overlap_chunks):
+            raise ValueError(f"overlap_chunks {overlap_chunks} must cut H = {H} into multiples of 256")
+        self.overlap_chunks, self.fc2_grid_cap = overlap_chunks, fc2_grid_cap
         self.ops = ops or GpuOps(device)
+        self._side = None
         self.timing = None  # (dispatch_ms, combine_ms) of the last forward when events are given
 
     def _route(self, idx):
@@ -298,17 +346,44 @@ class EPMoELayer:
         tb = ops.tables(ids, El + self.shared, 128)
         qp, sfp = ops.unpack_k(recv, R_all, H, K, tb)
         out_rows = ops.return_rows(tb, R_all, K)         # results in (row, pick) order: returned picks, shared
-        y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, P_all, events, out_rows=out_rows)
-        back = torch.empty((T * K, H), dtype=y.dtype, device=y.device)
-        if events:
-            events["combine"][0].record()
-        self._a2a(back, y[:P_recv], sc_picks, rc_picks)
-        if events:
-            events["combine"][1].record()
         self.last = {"received_rows": R_recv, "received_picks": P_recv, "sent_rows": sum(sc_rows),
                      "sent_picks": T * K, "tables": tb}
-        shared_rows = y[P_recv:P_all] if self.shared else None
-        return ops.combine(back, send_pos, wts, shared_rows, T, K, H)
+        C = self.overlap_chunks
+        if C == 1:
+            y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, P_all, events, out_rows=out_rows)
+            back = torch.empty((T * K, H), dtype=y.dtype, device=y.device)
+            if events:
+                events["combine"][0].record()
+            self._a2a(back, y[:P_recv], sc_picks, rc_picks)
+            if events:
+                events["combine"][1].record()
+            shared_rows = y[P_recv:P_all] if self.shared else None
+            return ops.combine(back, send_pos, wts, shared_rows, T, K, H)
+        # FC2 in C column slices; each slice's results go back on a side stream while the next one computes
+        if events:
+            events["fc1"][0].record()
+        f1q, f1sf = ops.fc1(self.w, qp, sfp, tb, H, self.I, El + self.shared)
+        if events:
+            events["fc1"][1].record()
+        cc = H // C
+        y = torch.empty((C, max(P_all, 1), cc), dtype=torch.bfloat16, device=qp.device)
+        back = torch.empty((C, T * K, cc), dtype=torch.bfloat16, device=qp.device)
+        if self._side is None:
+            self._side = ops.side_stream()
+        side = self._side
+        for j in range(C):
+            ops.fc2_cols(self.w, f1q, f1sf, tb, H, self.I, El + self.shared, out_rows, y[j], j * cc, cc,
+                         self.fc2_grid_cap)
+            ops.after(side)
+            with ops.on(side):
+                if events and j == 0:
+                    events["combine"][0].record()
+                self._a2a(back[j], y[j, :P_recv], sc_picks, rc_picks)
+                if events and j == C - 1:
+                    events["combine"][1].record()
+        ops.join(side, y, back)
+        shared_rows = y[:, P_recv:P_all] if self.shared else None
+        return ops.combine_chunked(back, send_pos, wts, shared_rows, T, K, H)
 
 
 def slice_weights(w13, w13_sf, w2, w2_sf, E, shared, rank, world, H, I, owner=None):

@@ -167,6 +167,41 @@ class OracleOps:
                 y[rmap[r]] = yp[r]
         return _bf16(y)
 
+    def fc1(self, w, qp, sfp, tb, H, I, n_experts):
+        nne = int(tb.meta[0])
+        wn = {k: _np(v) for k, v in w.items()}
+        return oracle.fc1(wn["w13"], wn["w13_sf"], qp, sfp, tb.cta_batch, tb.cta_limit, 0, nne, H, I)
+
+    def fc2_cols(self, w, f1q, f1sf, tb, H, I, n_experts, out_rows, out, col0, ncols, grid_cap=0):
+        nne = int(tb.meta[0])
+        wn = {k: _np(v) for k, v in w.items()}
+        yp = oracle.fc2(wn["w2"], wn["w2_sf"], f1q, f1sf, tb.cta_batch, tb.cta_limit, 0, nne, H, I)
+        o = _bits(out)  # a view: writes land in `out`
+        rmap = _np(out_rows)
+        for c in range(nne):
+            for r in range(c * 128, int(tb.cta_limit[c])):
+                o[rmap[r]] = yp[r, col0:col0 + ncols]
+
+    # no streams on the CPU: the side stream is the main one
+    def side_stream(self):
+        return None
+
+    def after(self, side):
+        pass
+
+    def on(self, side):
+        import contextlib
+
+        return contextlib.nullcontext()
+
+    def join(self, side, *tensors):
+        pass
+
+    def combine_chunked(self, back, send_pos, wts, shared_rows, T, K, H):
+        whole = torch.cat(list(back), dim=1)  # [rows, H]: the chunks side by side again
+        sh = torch.cat(list(shared_rows), dim=1) if shared_rows is not None else None
+        return self.combine(whole, send_pos, wts, sh, T, K, H)
+
     def combine(self, back, send_pos, wts, shared_rows, T, K, H):
         fc2 = _bits(back)
         meta = None

@@ -26,8 +26,12 @@ CFG = dict(T=96, H=256, I=256, E=8, K=2, shared=1, rs=2.5, seed=11)
 CFG_DENSE = dict(T=64, H=256, I=256, E=8, K=4, shared=1, rs=2.5, seed=12)
 
 
+# FC2 in two 256-column slices
+CFG_OVERLAP = dict(T=64, H=512, I=256, E=8, K=2, shared=1, rs=2.5, seed=13)
+
+
 def _cfg(mode):
-    return CFG_DENSE if mode == "dense" else CFG
+    return {"dense": CFG_DENSE, "overlap": CFG_OVERLAP}.get(mode, CFG)
 
 
 def _worker(rank, world, port, outdir, mode):
@@ -54,19 +58,21 @@ def _worker(rank, world, port, outdir, mode):
                                owner=owner)
     rs = t(np.array([c.rs_bits], np.uint16)).view(torch.bfloat16)
     layer = k3moe_ep.EPMoELayer(c.H, c.I, c.E, c.K, c.shared, w, t(c.bias), rs, ops=ep_oracle_ops.OracleOps(),
-                                fixed_tokens=T_l if mode == "fixed" else None, owner=owner)
+                                fixed_tokens=T_l if mode == "fixed" else None, owner=owner,
+                                overlap_chunks=2 if mode == "overlap" else 1)
     out = layer.forward(t(c.S[rows]), t(c.x_bits[rows]).view(torch.bfloat16))
     np.save(os.path.join(outdir, f"out{rank}.npy"), out.view(torch.int16).numpy().view(np.uint16))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "dense", "fixed", "placed"])
+@pytest.mark.parametrize("mode", ["counts", "dense", "fixed", "placed", "overlap"])
 def test_ep2_gloo_matches_single_device(mode):
     # counts / dense: one dispatched row a (token, rank) pair, headed by the token's picks there (dense: top-4
     # of 8 experts, so most rows carry several); fixed: the fixed-block all-to-all (no counts exchange, empty
     # slots marked -1) of decode-sized batches; placed: experts dealt to the ranks by router bias
-    # (balanced_owner) instead of in contiguous blocks
+    # (balanced_owner) instead of in contiguous blocks; overlap: FC2 in two column slices, each returned by
+    # its own all-to-all
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:

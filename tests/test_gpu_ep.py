@@ -61,7 +61,9 @@ def _worker(rank, world, port, outdir, mode):
     owner = k3moe_ep.balanced_owner(bias, world) if mode == "placed" else None
     w = k3moe_ep.slice_weights(w13, w13_sf, w2, w2_sf, E, sh, rank, world, H, I, owner=owner)
     layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev,
-                                fixed_tokens=c["T_local"] if mode in ("fixed", "graph") else None, owner=owner)
+                                fixed_tokens=c["T_local"] if mode in ("fixed", "graph") else None, owner=owner,
+                                overlap_chunks=2 if mode == "overlap" else 1,
+                                fc2_grid_cap=100 if mode == "overlap" else 0)
     xs, Ss = x[rows].contiguous(), S[rows].contiguous()
     graph = None
     if mode == "graph":
@@ -103,7 +105,7 @@ def _worker(rank, world, port, outdir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed"])
+@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed", "overlap"])
 def test_ep2_nccl_bit_identical_to_one_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
