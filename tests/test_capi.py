@@ -60,3 +60,26 @@ def test_bad_arguments_rejected_without_device_work(lib):
     assert lib.k3moe_route_topk(None, 2048, None, None, 8, 2048, 8, None, None, None) == -1
     assert lib.k3moe_quant_mxfp8(None, 100, 4, 100, None, None, 0, None) == -1
     assert lib.k3moe_layer_forward(None, None, 0, None) == -1
+
+
+def test_ep_and_gemm_argument_checks(lib):
+    # the pair-row stride: E4M3 row, scales, K int16 ids, 16-byte rows
+    assert lib.k3moe_ep_pair_row_stride(7168, 8) == 7408
+    assert lib.k3moe_ep_pair_row_stride(7168, 16) == 7424
+    assert lib.k3moe_ep_pair_row_stride(7168, 17) == 0 and lib.k3moe_ep_pair_row_stride(100, 8) == 0
+    # more ranks than a warp's lanes, K out of range, a stride too small for the ids: rejected before any launch
+    assert lib.k3moe_ep_pairs(None, 4, 8, 33, None, None) == -1
+    assert lib.k3moe_ep_pairs(None, 4, 17, 8, None, None) == -1
+    assert lib.k3moe_ep_pack_pairs(None, 7168, 4, 7168, 8, None, None, None, 1, 0, None, 7392, None) == -1
+    assert lib.k3moe_ep_ids_k(None, 7392, 4, 7168, 8, None, None) == -1
+    assert lib.k3moe_ep_unpack_k(None, 7408, 4, 7168, 0, None, None, None, None) == -1
+    assert lib.k3moe_ep_return_rows(None, 4, 8, None, None) == -1
+    # FC2 column slices: not on 256-column blocks, past H, a row stride shorter than the slice
+    args = [None] * 9
+    assert lib.k3moe_fc2_cols(*args, 1024, 128, 256, 7168, 2048, 8, 1024, 8, 0, None, None) == -1
+    assert lib.k3moe_fc2_cols(*args, 1024, 7168, 256, 7168, 2048, 8, 1024, 8, 0, None, None) == -1
+    assert lib.k3moe_fc2_cols(*args, 128, 0, 256, 7168, 2048, 8, 1024, 8, 0, None, None) == -1
+    # the GEMM outputs must start 32-byte aligned (the epilogues store 32 bytes at a time)
+    assert lib.k3moe_fc2(None, None, None, None, None, None, None, 16, 7168, 2048, 8, 1024, 8, None, None) == -1
+    assert lib.k3moe_combine_ep_chunked(None, 0, 100, None, None, None, 0, 0, None, 7168, 4, 8, 7168, 1000,
+                                        None) == -1
