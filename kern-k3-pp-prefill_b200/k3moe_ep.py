@@ -231,6 +231,8 @@ class EPMoELayer:
         self.world = dist.get_world_size(group)
         if E % self.world:
             raise ValueError(f"{E} experts do not split over {self.world} ranks")
+        if self.world > 16 and fixed_tokens is None:
+            raise ValueError("the (token, rank) pair plan is a routing table of one column a rank: at most 16 ranks")
         self.H, self.I, self.E, self.K, self.shared = H, I, E, K, int(shared)
         self.E_local = E // self.world
         self.w, self.bias, self.rs = w, bias, rs
