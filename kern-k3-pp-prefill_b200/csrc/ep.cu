@@ -4,7 +4,7 @@
 // replicates the batch and all-reduces, roofline/decode.md:164-166; this is the
 // token-sharded layout of the benchmark configurations.)
 //
-// Packed row (dispatch wire format), `stride` = roundup(H + H/32 + 4, 16) bytes:
+// One row a pick (the fixed-block dispatch of decode-sized batches), `stride` = roundup(H + H/32 + 4, 16) bytes:
 //   [0, H)            E4M3 elements (MXFP8, the rule of k3moe_quant_mxfp8)
 //   [H, H + H/32)     UE8M0 scale per 32 elements, linear
 //   [H + H/32, +4)    local expert id at the destination (int32)
