@@ -66,17 +66,11 @@ def _worker(rank, world, port, outdir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "dense", "fixed", "placed", "overlap"])
-def test_ep2_gloo_matches_single_device(mode):
-    # counts / dense: one dispatched row a (token, rank) pair, headed by the token's picks there (dense: top-4
-    # of 8 experts, so most rows carry several); fixed: the fixed-block all-to-all (no counts exchange, empty
-    # slots marked -1) of decode-sized batches; placed: experts dealt to the ranks by router bias
-    # (balanced_owner) instead of in contiguous blocks; overlap: FC2 in two column slices, each returned by
-    # its own all-to-all
+def _run(world, mode):
     ctx = mp.get_context("spawn")
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
-        procs = [ctx.Process(target=_worker, args=(r, 2, port, d, mode)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, world, port, d, mode)) for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
@@ -84,7 +78,26 @@ def test_ep2_gloo_matches_single_device(mode):
             if p.is_alive():
                 p.kill()
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-        got = np.concatenate([np.load(os.path.join(d, f"out{r}.npy")) for r in range(2)])
+        return np.concatenate([np.load(os.path.join(d, f"out{r}.npy")) for r in range(world)])
+
+
+@pytest.mark.parametrize("mode", ["counts", "placed"])
+def test_ep4_gloo_matches_single_device(mode):
+    """Four ranks (two experts each): the pair plan and the counts exchange over more than two ranks."""
+    got = _run(4, mode)
+    c = cases.make_case(**_cfg(mode))
+    ref, _ = cases.oracle_forward(c)
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("mode", ["counts", "dense", "fixed", "placed", "overlap"])
+def test_ep2_gloo_matches_single_device(mode):
+    # counts / dense: one dispatched row a (token, rank) pair, headed by the token's picks there (dense: top-4
+    # of 8 experts, so most rows carry several); fixed: the fixed-block all-to-all (no counts exchange, empty
+    # slots marked -1) of decode-sized batches; placed: experts dealt to the ranks by router bias
+    # (balanced_owner) instead of in contiguous blocks; overlap: FC2 in two column slices, each returned by
+    # its own all-to-all
+    got = _run(2, mode)
     c = cases.make_case(**_cfg(mode))
     ref, _ = cases.oracle_forward(c)
     assert np.array_equal(got, ref)
