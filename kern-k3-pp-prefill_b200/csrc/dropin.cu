@@ -16,6 +16,7 @@
 //   kern_k3g_moe_finalize_rms   source/k3_moe_route.cu:538    grid rows, block 448
 //   kern_k3g_moe_route          source/k3_moe_route.cu:338    grid 64 (B <= 256) or 288, block 512 (grid barrier)
 //   kern_k3g_moe_route_init     source/k3_moe_route.cu:522    any grid, block 1024
+//   kern_k3g_situ               source/k3_prefill_glue.cu:668 grid (B, ceil(n/2048)), block 256
 //   kern_k3_moe_w_shuffle       source/k3_moe_prefill.cu:242  grid ceil(experts*n*row_bytes/16/block)
 //   kern_k3_moe_sf_shuffle      source/k3_moe_prefill.cu:252  grid ceil(experts*n*kg/block)
 //   kern_k3_moe_front           source/k3_moe_front.cu:358    grid T + NSH/64 (T <= 64), block 1024, F_SMEM
@@ -482,6 +483,28 @@ extern "C" __global__ void __launch_bounds__(dropin::RT_THREADS, 2) kern_k3g_moe
 // kern_k3g_moe_route_init (source/k3_moe_route.cu:522): zero the sync words before a stage's first call
 extern "C" __global__ void __launch_bounds__(1024) kern_k3g_moe_route_init(u32* __restrict__ sync) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dropin::SYNC_WORDS; i += gridDim.x * blockDim.x) sync[i] = 0u;
+}
+
+// K3's shared-expert SiTU on landed bf16 operands (kern_k3g_situ, source/k3_prefill_glue.cu:668-686): p = [gate |
+// up] rows of 2n bf16, act [B, n] bf16.  Grid (B, ceil(n / 2048)), block 256, 8 columns a thread (n a
+// multiple of 8); the fused front's arithmetic (situ_front).
+extern "C" __global__ void __launch_bounds__(256) kern_k3g_situ(const bf16* __restrict__ p, bf16* __restrict__ act,
+                                                                 int n, int B) {
+  const int b = blockIdx.x;
+  const int j = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (b >= B || j >= n) return;
+  const uint4 gv = *reinterpret_cast<const uint4*>(p + (long long)b * 2 * n + j);
+  const uint4 uv = *reinterpret_cast<const uint4*>(p + (long long)b * 2 * n + n + j);
+  const u32* gp = reinterpret_cast<const u32*>(&gv);
+  const u32* up = reinterpret_cast<const u32*>(&uv);
+  uint4 o;
+  u32* op = reinterpret_cast<u32*>(&o);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const float2 g2 = bf16x2_to_f2(gp[l]), u2 = bf16x2_to_f2(up[l]);
+    op[l] = f2_to_bf16x2(situ_front(g2.x, u2.x), situ_front(g2.y, u2.y));
+  }
+  *reinterpret_cast<uint4*>(act + (long long)b * n + j) = o;
 }
 
 // ------------------------------------------------------------------ load-time weight re-layouts

@@ -402,3 +402,24 @@ def test_decode_front_latency(dev, front_weights, capsys):
         print("\nkern_k3_moe_front device time a launch (us): rows, reference, k3moe")
         for T, r, k in rows:
             print(f"  {T:3d}  {r:7.2f}  {k:7.2f}")
+
+
+@pytest.mark.parametrize("B,n", [(1, 768), (37, 6144), (5, 1032)])
+def test_situ(dev, B, n):
+    """kern_k3g_situ: K3's shared-expert SiTU on bf16 [gate | up] rows, byte-equal to the reference entry,
+    including gates below -87 (where the reference leaves its fast reciprocal for the IEEE one)."""
+    rng = np.random.default_rng(B * n)
+    p = (4.0 * rng.standard_normal((B, 2 * n))).astype(np.float32)
+    p[:, : min(16, n)] = -100.0
+    pb = _t(oracle.bf16_bits(p), dev).view(torch.bfloat16)
+
+    def mk():
+        out = _poison((B, n), torch.bfloat16, dev)
+        return [rk.P(pb), rk.P(out), rk.I(n), rk.I(B)], out
+
+    grid = (B, -(-n // 2048), 1)
+    ro, o = _both("k3_prefill_glue", "kern_k3g_situ", grid, (256, 1, 1), mk)
+    assert torch.equal(o.view(torch.int16), ro.view(torch.int16))
+    land = oracle.bf16_to_f32(oracle.bf16_bits(p))
+    want = oracle.situ(land[:, :n], land[:, n:])
+    assert np.allclose(o.float().cpu().numpy(), want, rtol=1.6e-2, atol=1e-3)
