@@ -8,6 +8,7 @@
 //   kern_k3_moe_quant           source/k3_moe_prefill.cu:66   grid ceil(rows*cols/32/256), block 256
 //   kern_k3_mxfp8_quant         source/k3_mxfp8.cu:20         any grid, block 256
 //   kern_k3g_router_topk        source/k3_prefill_glue.cu:504 grid ceil(B/4), block 128 (E = 896)
+//   kern_k3_router_topk         source/k3_router_argmax.cu:110 grid B, block 1024 (E = 896)
 //   kern_k3_moe_route_count     source/k3_moe_prefill.cu:97   grid ceil(T/256), block 256
 //   kern_k3_moe_route_tables    source/k3_moe_prefill.cu:115  grid 1, block 1024
 //   kern_k3_moe_route_scatter   source/k3_moe_prefill.cu:155  grid ceil(T/256), block 256
@@ -97,6 +98,23 @@ extern "C" __global__ void __launch_bounds__(128) kern_k3g_router_topk(const flo
   topk_warp<dropin::N_EXPERTS / 32>(S + (long long)b * dropin::N_EXPERTS, bias, dropin::N_EXPERTS, dropin::TOPK,
                                   __bfloat162float(rs[0]), threadIdx.x & 31, ck[warp], ce[warp],
                                   idx + (long long)b * dropin::TOPK, wts + (long long)b * dropin::TOPK);
+}
+
+// kern_k3_router_topk (source/k3_router_argmax.cu:110-206): the decode router's top-16 of S [B, 896], one block
+// a row, grid (B), block 1024 (the reference's launch: the experts rounded up to 256); warp 0 runs the same
+// selection as kern_k3g_router_topk, so the picks and weight bits are that entry's.
+extern "C" __global__ void __launch_bounds__(1024, 1) kern_k3_router_topk(const float* __restrict__ S,
+                                                                          const float* __restrict__ bias,
+                                                                          const bf16* __restrict__ rs,
+                                                                          int* __restrict__ idx, float* __restrict__ wts,
+                                                                          int B) {
+  __shared__ u32 ck[TOPK_CAND];
+  __shared__ int ce[TOPK_CAND];
+  const int b = blockIdx.x;
+  if (b >= B || threadIdx.x >= 32) return;
+  topk_warp<dropin::N_EXPERTS / 32>(S + (long long)b * dropin::N_EXPERTS, bias, dropin::N_EXPERTS, dropin::TOPK,
+                                    __bfloat162float(rs[0]), threadIdx.x, ck, ce, idx + (long long)b * dropin::TOPK,
+                                    wts + (long long)b * dropin::TOPK);
 }
 
 // ------------------------------------------------------------------ EP-slice routing tables (top-16)

@@ -423,3 +423,20 @@ def test_situ(dev, B, n):
     land = oracle.bf16_to_f32(oracle.bf16_bits(p))
     want = oracle.situ(land[:, :n], land[:, n:])
     assert np.allclose(o.float().cpu().numpy(), want, rtol=1.6e-2, atol=1e-3)
+
+
+@pytest.mark.parametrize("B", [1, 7, 64])
+def test_decode_router_topk(dev, B):
+    """kern_k3_router_topk (the decode router's entry, one block a row): ids and weight bits byte-equal to the
+    reference entry's."""
+    rng = np.random.default_rng(100 + B)
+    S = _t((2.0 * rng.standard_normal((B, E))).astype(np.float32), dev)
+    bias = _t(rng.uniform(-0.1, 0.1, E).astype(np.float32), dev)
+    rs = _t(oracle.bf16_bits(np.array([2.5], np.float32)), dev).view(torch.bfloat16)
+
+    def mk():
+        i, w = _poison((B, TOPK), torch.int32, dev), _poison((B, TOPK), torch.float32, dev)
+        return [rk.P(S), rk.P(bias), rk.P(rs), rk.P(i), rk.P(w), rk.I(B)], (i, w)
+
+    (ri, rw), (i, w) = _both("k3_router_argmax", "kern_k3_router_topk", (B, 1, 1), (1024, 1, 1), mk)
+    assert torch.equal(i, ri) and torch.equal(w.view(torch.int32), rw.view(torch.int32))
