@@ -8,17 +8,25 @@ FC2 (bf16) -> routing-weighted combine, plus the always-on shared expert.
 Shapes: T=8192 (16 packed sequences, Dirichlet lengths), H=7168, I=2048,
 E=896 routed experts, top-8, routed scale 2.5, shared expert width 2048; all
 expert weights MXFP4 (20.96 GB), synthetic and seeded (no checkpoint, no
-dataset).  The router logits S = x.W_router are computed once before timing
-(the router GEMM is the layer before this path).
+dataset).  The inputs (x, router weight, bias) are made on the host with
+numpy from fixed seeds, the same in both arms, and the router logits
+S = x.W_router are computed once before timing (the router GEMM is the layer
+before this path).
 
 `value` is device-resident throughput (tokens/s over all ranks); `e2e` is the
 same layer through the public API with x and S copied from pinned host memory
-and the output copied back inside every timed step.  With N > 1 the layer is
+and the output copied back inside every timed step.  After timing, the CPU leg
+checks the run's own intermediates against the CPU restatement (`parity`:
+routing and quantisation bit for bit, FC1 / FC2 on sampled token tiles within
+tolerance, the combine of sampled tokens bit for bit) and times that
+restatement's FC1 + FC2 on the sample (`cpu_baseline`).  With N > 1 the layer is
 expert parallel (config 4's layout): every rank owns an 8192-row chunk and
 896/N experts (+ the shared expert), tokens travel to their experts' ranks and
-back by NCCL all-to-all (timed separately), weak scaling.  `--impl reference` times the
-CPU restatement of the same path (oracle/, the reference's algorithm) on a
-bounded sample on the host cores.
+back by NCCL all-to-all (timed separately), weak scaling; every rank then
+checks its output bytes against the 1-GPU layer over all experts
+(`ep_bit_identical`) and a config-2 decode step is timed at the same N
+(`decode`).  `--impl reference` times the CPU restatement of the same path
+(oracle/, the reference's algorithm) on a bounded sample on the host cores.
 """
 from __future__ import annotations
 
@@ -126,28 +134,85 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-# ------------------------------------------------------------------ CPU baseline (oracle port)
-def cpu_sample(sample_tiles, tb, wsrc, qsrc, threads=0):
-    """Time the oracle's FC1 + FC2 over `sample_tiles` token tiles (compact copies).
+# ------------------------------------------------------------------ inputs (both arms)
+def bf16_round(a):
+    """f32 -> bf16 bit patterns, round to nearest even (numpy)."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
 
-    tb: host tables (cta_batch, cta_limit); wsrc(e) -> (w13, w13_sf, w2, w2_sf) of expert e;
-    qsrc(c) -> (q rows [128, H], tiled sf of the tile).  Returns seconds."""
+
+def host_inputs(T, E, seed_x, seed_router=7):
+    """The layer's inputs, made on the host with numpy so both arms (the GPU arm and the CPU reference arm) route
+    the same rows: x bf16 [T, H] ~ N(0, 1) (bit patterns), router weight [H, E] ~ N(0, 1/H) and S = x.W_router
+    in f32, bias ~ U(-0.1, 0.1), rs = 2.5 (bf16 bits).  The router weight and bias are the same on every rank."""
+    rng = np.random.default_rng(seed_x)
+    x_bits = bf16_round(rng.standard_normal((T, H), dtype=np.float32))
+    rr = np.random.default_rng(seed_router)
+    wr = rr.standard_normal((H, E), dtype=np.float32) / np.float32(np.sqrt(H))
+    bias = rr.uniform(-0.1, 0.1, E).astype(np.float32)
+    xf = (x_bits.astype(np.uint32) << 16).view(np.float32)
+    S = np.ascontiguousarray(xf @ wr, dtype=np.float32)
+    return {"x_bits": x_bits, "S": S, "bias": bias, "rs_bits": int(bf16_round(np.array([RS], np.float32))[0])}
+
+
+def device_inputs(h, dev):
+    import torch
+
+    x = torch.from_numpy(h["x_bits"].view(np.int16)).to(dev).view(torch.bfloat16)
+    S = torch.from_numpy(h["S"]).to(dev)
+    bias = torch.from_numpy(h["bias"]).to(dev)
+    rs = torch.from_numpy(np.array([h["rs_bits"]], np.uint16).view(np.int16)).to(dev).view(torch.bfloat16)
+    return x, S, bias, rs
+
+
+def host_threads():
+    """The host threads this process may run on (its CPU affinity), used explicitly by the CPU legs (torchrun
+    sets OMP_NUM_THREADS=1, which the CPU restatement would otherwise inherit)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def sample_tiles_of(nne, n):
+    return sorted(set(np.linspace(0, nne - 1, n).astype(int).tolist()))
+
+
+def tm_rows(block, K):
+    """A 128-row block of a tile-major operand (K/128 tiles of 128 x 128 bytes) -> row-major [128, K]."""
+    return np.ascontiguousarray(block.reshape(K // 128, 128, 128).transpose(1, 0, 2).reshape(128, K))
+
+
+def rows_tm(rows128, K):
+    """Row-major [128, K] -> one 128-row block of a tile-major operand (bytes)."""
+    return np.ascontiguousarray(rows128.reshape(128, K // 128, 128).transpose(1, 0, 2).reshape(128, K))
+
+
+# ------------------------------------------------------------------ the CPU leg: oracle as checker and as CPU baseline
+def oracle_ffn(tiles, cta_batch, cta_limit, wsrc, qsrc, f1src=None):
+    """The CPU restatement's FC1 + FC2 over token tiles `tiles` of a layer, on compact copies (tile i of the
+    sample at rows [128 i, 128 i + 128)).  wsrc(e) -> (w13, w13_sf, w2, w2_sf) of expert e (tile-major bytes);
+    qsrc(c) -> (q block [128, H] tile-major, its tiled scales).  FC2 reads FC1's output bytes from f1src(c) ->
+    (block [128, I] tile-major, scales) when given (the device's own, for a check of FC2 alone), else the
+    oracle's FC1 output.  Returns (FC1 q, FC1 sf, FC2 bf16 bits [ns*128, H], real rows a tile, seconds of the
+    FC1 + FC2 calls)."""
     import oracle
 
-    oracle.set_threads(threads)
-    ns = len(sample_tiles)
-    kg4 = H // 128
+    ns = len(tiles)
+    kg4, ig4 = H // 128, I // 128
     qp = np.zeros((ns * 128, H), np.uint8)
     sfp = np.zeros(ns * kg4 * 512, np.uint8)
     w13 = np.zeros((ns * 2 * I, H // 2), np.uint8)
     w13sf = np.zeros(ns * 2 * I // 128 * kg4 * 512, np.uint8)
     w2 = np.zeros((ns * H, I // 2), np.uint8)
-    w2sf = np.zeros(ns * H // 128 * (I // 128) * 512, np.uint8)
+    w2sf = np.zeros(ns * H // 128 * ig4 * 512, np.uint8)
     cb = np.arange(ns, dtype=np.int32)
     cl = np.zeros(ns, np.int32)
-    for i, c in enumerate(sample_tiles):
-        e = int(tb["cta_batch"][c])
-        n = int(tb["cta_limit"][c]) - c * 128
+    n_real = []
+    for i, c in enumerate(tiles):
+        e = int(cta_batch[c])
+        n = int(cta_limit[c]) - c * 128
+        n_real.append(n)
         cl[i] = i * 128 + n
         q, sf = qsrc(c)
         qp[i * 128:(i + 1) * 128] = q
@@ -159,38 +224,162 @@ def cpu_sample(sample_tiles, tb, wsrc, qsrc, threads=0):
         w2sf[i * len(bsf):(i + 1) * len(bsf)] = bsf
     t0 = time.perf_counter()
     f1q, f1sf = oracle.fc1(w13, w13sf, qp, sfp, cb, cl, 0, ns, H, I)
-    oracle.fc2(w2, w2sf, f1q, f1sf, cb, cl, 0, ns, H, I)
-    return time.perf_counter() - t0
+    t1 = time.perf_counter()
+    if f1src is not None:
+        dq = np.zeros_like(f1q)
+        dsf = np.zeros_like(f1sf)
+        for i, c in enumerate(tiles):
+            a, s = f1src(c)
+            dq[i * 128:(i + 1) * 128] = a
+            dsf[i * ig4 * 512:(i + 1) * ig4 * 512] = s
+        src_q, src_sf = dq, dsf
+    else:
+        src_q, src_sf = f1q, f1sf
+    t2 = time.perf_counter()
+    y = oracle.fc2(w2, w2sf, src_q, src_sf, cb, cl, 0, ns, H, I)
+    t3 = time.perf_counter()
+    return f1q, f1sf, y, n_real, (t1 - t0) + (t3 - t2)
 
 
-def cpu_topk_time(S, bias, rs_bits):
+def inrun_parity(layer, host, w, out, T, E, tiles, n_tokens=64):
+    """The 1-GPU arm's check of its own timed run (after timing, outside the timed region): the run's
+    intermediates, read back from the layer's workspace, against the CPU restatement on the same inputs.
+    Bit-exact: router ids and weights (all rows), routing tables, the MXFP8 rows and scales of the sampled
+    token tiles, the combine of `n_tokens` tokens (from the device's own FC2 rows).  Tolerance (rel-L2 <= 1e-2,
+    max-abs <= 2e-2 widened per element to 3 bf16 ulp + 1e-3 as cases.within_contract): FC1 (dequantised
+    MXFP8 out) and FC2 (bf16, from the device's own FC1 bytes) over the sampled tiles.  Also returns the CPU
+    seconds of top-k (all rows) and of FC1 + FC2 over the tiles: the CPU baseline's sample."""
+    import torch
+
+    import cases
     import oracle
 
+    off = layer.offsets(T)
+    ws = layer.ws
+    K_ = layer.K
+
+    def get(name, nbytes, dtype=np.uint8, at=0):
+        return ws[off[name] + at:off[name] + at + nbytes].cpu().numpy().view(dtype)
+
+    meta = get("meta", 16, np.int32)
+    nne, total_padded = int(meta[0]), int(meta[1])
+    d_idx = get("idx", T * K_ * 4, np.int32).reshape(T, K_)
+    d_wts = get("wts", T * K_ * 4, np.int32).reshape(T, K_)
     t0 = time.perf_counter()
-    oracle.topk(S, bias, rs_bits, K)
-    return time.perf_counter() - t0
+    o_idx, o_wts = oracle.topk(host["S"], host["bias"], host["rs_bits"], K_)
+    t_topk = time.perf_counter() - t0
+    res = {"topk_equal": bool(np.array_equal(d_idx, o_idx) and np.array_equal(d_wts, o_wts.view(np.int32)))}
+    tb = oracle.tables(o_idx, E, 0, SHARED)
+    cb = get("cta_batch", nne * 4, np.int32)
+    cl = get("cta_limit", nne * 4, np.int32)
+    e2p = get("exp2perm", T * K_ * 4, np.int32).reshape(T, K_)
+    res["tables_equal"] = bool(
+        np.array_equal(get("counts", (E + SHARED) * 4, np.int32), tb["counts"]) and
+        np.array_equal(meta[:3], tb["meta"][:3]) and np.array_equal(cb, tb["cta_batch"][:nne]) and
+        np.array_equal(cl, tb["cta_limit"][:nne]) and
+        np.array_equal(get("route_map", total_padded * 4, np.int32), tb["route_map"][:total_padded]) and
+        np.array_equal(e2p, tb["exp2perm"]))
+    kg4, ig4 = H // 128, I // 128
+    route_map = tb["route_map"]
+    quant_ok = True
+
+    def qsrc(c):
+        nonlocal quant_ok
+        q = get("q_perm", 128 * H, at=c * 128 * H).reshape(128, H)
+        sf = get("sf_perm", kg4 * 512, at=c * kg4 * 512)
+        n = int(cl[c]) - c * 128
+        oq, osf = oracle.quant_mxfp8(host["x_bits"][route_map[c * 128:c * 128 + n]], tiled=True)
+        real = np.zeros(kg4 * 512, bool)  # the scale bytes of the real rows
+        r = np.arange(n)[:, None]
+        kb = np.arange(H // 32)[None, :]
+        real[((r // 128) * kg4 + kb // 4) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + kb % 4] = True
+        quant_ok &= bool(np.array_equal(tm_rows(q, H)[:n], oq) and np.array_equal(sf[real], osf[real]))
+        return q, sf
+
+    per13 = 2 * I // 128 * kg4 * 512
+    per2 = H // 128 * ig4 * 512
+
+    def wsrc(e):
+        return (w["w13"][e * 2 * I:(e + 1) * 2 * I].cpu().numpy(), w["w13_sf"][e * per13:(e + 1) * per13].cpu().numpy(),
+                w["w2"][e * H:(e + 1) * H].cpu().numpy(), w["w2_sf"][e * per2:(e + 1) * per2].cpu().numpy())
+
+    def f1src(c):
+        return get("fc1_q", 128 * I, at=c * 128 * I).reshape(128, I), get("fc1_sf", ig4 * 512, at=c * ig4 * 512)
+
+    f1q, f1sf, y, n_real, t_ffn = oracle_ffn(tiles, cb, cl, wsrc, qsrc, f1src)
+    res["quant_tiles_equal"] = quant_ok
+    rows = np.concatenate([np.arange(i * 128, i * 128 + n) for i, n in enumerate(n_real)])
+    dq = np.concatenate([f1src(c)[0] for c in tiles])
+    dsf = np.concatenate([f1src(c)[1] for c in tiles])
+    got1 = oracle.dequant_rows(dq, dsf, rows)
+    ref1 = oracle.dequant_rows(f1q, f1sf, rows)
+    ok1, rel1, ratio1 = cases.within_contract(got1, ref1)
+    res["fc1"] = {"rel_l2": rel1, "max_abs": float(np.abs(got1 - ref1).max()), "worst_vs_bound": ratio1,
+                  "e4m3_bytes_differing": float(np.mean(tm_rows_all(dq, I, rows) != tm_rows_all(f1q, I, rows))),
+                  "ok": bool(ok1)}
+    dfc2 = np.concatenate([get("fc2", 128 * H * 2, np.uint16, at=c * 128 * H * 2).reshape(128, H) for c in tiles])
+    got2, ref2 = oracle.bf16_to_f32(dfc2[rows]), oracle.bf16_to_f32(y[rows])
+    ok2, rel2, ratio2 = cases.within_contract(got2, ref2)
+    res["fc2"] = {"rel_l2": rel2, "max_abs": float(np.abs(got2 - ref2).max()), "worst_vs_bound": ratio2,
+                  "ok": bool(ok2)}
+    # the combine of n_tokens tokens from the device's own FC2 rows: bit-exact
+    toks = sample_tiles_of(T, n_tokens)
+    nt = len(toks)
+    prow = e2p[toks]                                   # [nt, K] permuted rows
+    srow = int(meta[2]) + np.asarray(toks) if SHARED else None
+    gather = np.concatenate([prow.reshape(-1)] + ([srow] if SHARED else [])).astype(np.int64)
+    fc2_all = ws[off["fc2"]:off["fc2"] + total_padded * H * 2].view(torch.int16).view(-1, H)
+    fc2rows = torch.index_select(fc2_all, 0, torch.from_numpy(gather).to(ws.device)).cpu().numpy().view(np.uint16)
+    ce2p = np.where(prow >= 0, np.arange(nt * K_).reshape(nt, K_), -1).astype(np.int32)
+    cmeta = np.array([0, 0, nt * K_ if SHARED else -1, 0], np.int32)
+    ocomb = oracle.combine(fc2rows, ce2p, d_wts[toks].view(np.float32), cmeta, nt, K_)
+    dout = out[toks].view(torch.int16).cpu().numpy().view(np.uint16)
+    res["combine_tokens_equal"] = bool(np.array_equal(ocomb, dout))
+    res["tiles"] = len(tiles)
+    res["combine_tokens"] = nt
+    res["ok"] = bool(res["topk_equal"] and res["tables_equal"] and quant_ok and ok1 and ok2 and
+                     res["combine_tokens_equal"])
+    return res, t_topk, t_ffn
 
 
-def sample_tiles_of(nne, n=16):
-    return sorted(set(np.linspace(0, nne - 1, n).astype(int).tolist()))
+def tm_rows_all(buf, K, rows):
+    """Rows `rows` of a compact tile-major operand [n*128, K] as row-major bytes."""
+    import oracle
+
+    return oracle.t128_rows(buf, rows, K)
 
 
 # ------------------------------------------------------------------ the reference arm (CPU)
+def ep_config(T, E, world, args):
+    return {"workload": f"K3-shape prefill MoE layer, expert parallel over {world} GPUs (config 4 layout)",
+            "T_per_gpu": T, "H": H, "I": I, "E": E, "E_per_gpu": E // world, "K": K, "shared_expert_width": I,
+            "rs": RS, "global_batch": T * world, "seq_len": T, "parallelism": f"ep{world}",
+            "expert_placement": args.ep_placement, "fc2_slices": args.ep_overlap, "fc2_grid_cap": args.ep_fc2_cap,
+            "l2": "inputs larger than L2: each GPU streams its experts' weights every step"}
+
+
 def run_reference(args):
+    """The reference's algorithm on the host cores: the CPU restatement (oracle/, kind "port") on the GPU arm's
+    own inputs (the same host generator and seeds, so the same routing and tiles).  A step times the router top-k
+    over every row plus FC1 + FC2 over `--cpu-tiles` token tiles spread over the layer (a bounded sample); the
+    value projects it to the whole layer (all its tiles).  With N > 1 rank 0 runs its own chunk of the
+    expert-parallel job (the host cores would run the N chunks one after another: the same tokens/s)."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import oracle
 
-    threads = oracle.set_threads(0)
-    T = args.tokens
-    rng = np.random.default_rng(0)
-    x_bits = oracle.bf16_bits(rng.standard_normal((T, H), dtype=np.float32))
-    wr = (rng.standard_normal((H, E), dtype=np.float32) / np.sqrt(H)).astype(np.float32)
-    S = (oracle.bf16_to_f32(x_bits) @ wr).astype(np.float32)
-    bias = rng.uniform(-0.1, 0.1, E).astype(np.float32)
-    rs_bits = int(oracle.bf16_bits(np.array([RS], np.float32))[0])
-    idx, wts = oracle.topk(S, bias, rs_bits, K)
+    threads = oracle.set_threads(host_threads())
+    T, E = args.tokens, args.experts
+    hin = host_inputs(T, E, 1000)
+    bias, zipf = hin["bias"], None
+    if args.zipf and world == 1:  # the GPU arm's config-3 bias, fitted on the same logits
+        import cases
+
+        bias, beta, kl = cases.zipf_bias(hin["S"], K)
+        zipf = {"s": 1.1, "seed": 3, "beta": beta, "kl": round(kl, 4)}
+    idx, wts = oracle.topk(hin["S"], bias, hin["rs_bits"], K)
     tb = oracle.tables(idx, E, 0, SHARED)
     nne = int(tb["meta"][0])
     tiles = sample_tiles_of(nne, args.cpu_tiles)
@@ -204,26 +393,35 @@ def run_reference(args):
         return wcache[e]
 
     def qsrc(c):
-        rows = tb["route_map"][c * 128:(c + 1) * 128]
-        q, sf = oracle.quant_mxfp8(x_bits[rows], tiled=True)
-        return q, sf
+        n = int(tb["cta_limit"][c]) - c * 128
+        rows = np.zeros(128, np.int64)
+        rows[:n] = tb["route_map"][c * 128:c * 128 + n]
+        q, sf = oracle.quant_mxfp8(hin["x_bits"][rows], tiled=True)
+        return rows_tm(q, H), sf
 
-    for e in {int(tb["cta_batch"][c]) for c in tiles}:
-        wsrc(e)
-    times = []
+    for c in tiles:
+        wsrc(int(tb["cta_batch"][c]))
+    step_s, layer_s = [], []
     for step in range(args.warmup + args.steps):
-        t = cpu_topk_time(S, bias, rs_bits) + cpu_sample(tiles, tb, wsrc, qsrc, threads) * nne / len(tiles)
+        t0 = time.perf_counter()
+        t1 = time.perf_counter()
+        oracle.topk(hin["S"], bias, hin["rs_bits"], K)
+        t_topk = time.perf_counter() - t1
+        t_ffn = oracle_ffn(tiles, tb["cta_batch"], tb["cta_limit"], wsrc, qsrc)[4]
         if step >= args.warmup:
-            times.append(t)
-    sec = statistics.mean(times)
+            step_s.append(time.perf_counter() - t0)
+            layer_s.append(t_topk + t_ffn * nne / len(tiles))
+    sec = statistics.mean(layer_s)
     value = T / sec
     sample = (f"router top-k over all {T} rows + oracle FC1+FC2 over {len(tiles)} of {nne} token tiles (spread "
-              f"evenly), scaled by {nne}/{len(tiles)}")
+              f"evenly), timed each step and projected to all {nne} tiles (whole layer {sec * 1e3:.0f} ms)")
+    config = prefill_config(T, E, zipf) if world == 1 else ep_config(T, E, world, args)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.mean(step_s) * 1e3,
+        "layer_ms_projected": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
-        "config": prefill_config(T, E, None),
+        "config": config, "routing": {"num_non_exiting": nne},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -320,35 +518,31 @@ def rank_experts(E, world, rank, bias, placement):
     return owner, (owner == rank).nonzero().flatten().tolist()
 
 
-def rank_inputs(T, E, rank, dev):
-    """bf16 x [T, H] ~ N(0, 1) of this rank, router logits S = x.W_router (W_router ~ N(0, 1/H), the same on
-    every rank), bias ~ U(-0.1, 0.1), rs."""
-    import torch
+def full_layer(E, bias, rs, T, dev):
+    """The 1-GPU layer over every expert (the same synthetic weight streams as the ranks' slices): the
+    expert-parallel arm's check that its output is the same bytes."""
+    import k3moe
 
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
-    x = torch.randn((T, H), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    g.manual_seed(7)
-    wr = torch.randn((H, E), generator=g, device=dev, dtype=torch.float32) / H ** 0.5
-    S = (x.float() @ wr).contiguous()
-    bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
-    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
-    return x, S, bias, rs
+    w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, (E + SHARED) * 2 * I, H, WSD, device=dev)
+    w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, (E + SHARED) * H, I, WSD, device=dev)
+    return k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
 
 
 # ------------------------------------------------------------------ the GPU arm, N > 1: expert parallel
 def run_ep(args, world, rank, dev):
     """Config 4's layout at N GPUs: every rank owns an 8192-row chunk (16 packed sequences) and E/N experts
-    (+ the shared expert); dispatch and combine are NCCL all-to-all; weak scaling (N x 8192 rows a step)."""
+    (+ the shared expert); dispatch and combine are NCCL all-to-all; weak scaling (N x 8192 rows a step).
+    After timing, every rank checks its output against the 1-GPU layer over all experts on its own rows
+    (`ep_bit_identical`, all ranks), and a config-2 decode step (64 tokens over the N ranks) is timed as a
+    CUDA graph and checked the same way (`decode`)."""
     import torch
     import torch.distributed as dist
 
-    import k3moe
     import k3moe_ep
 
     E, T = args.experts, args.tokens
     El = E // world
-    x, S, bias, rs = rank_inputs(T, E, rank, dev)
+    x, S, bias, rs = device_inputs(host_inputs(T, E, 1000 + rank), dev)
     owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
     w = rank_weights(E, mine, dev)
     layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, owner=owner,
@@ -388,6 +582,20 @@ def run_ep(args, world, rank, dev):
     counts = tb.counts.cpu().numpy()
     routed_rows, touched = int(counts.sum()), int((counts > 0).sum())
     fc1_bytes = touched * (2 * I * H // 2 + 2 * I * H // 32) + routed_rows * (H + H // 32 + I + I // 32)
+    # ---------------- the check (untimed): this rank's rows through the 1-GPU layer over all 896 experts
+    out_ep = layer.forward(S, x)
+    torch.cuda.synchronize()
+    full = full_layer(E, bias, rs, T, dev)
+    out_1 = full.forward(S, x)
+    torch.cuda.synchronize()
+    full.check_device_error(T)
+    same = torch.tensor([1 if torch.equal(out_ep.view(torch.int16), out_1.view(torch.int16)) else 0], device=dev)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    ep_identical = bool(same.item() == 1)
+    del out_1
+    # ---------------- config 2 at this N: a 64-token decode step, CUDA graph, checked against the full layer
+    dec = decode_pass(args, world, rank, dev, w, owner, full) if args.decode_tokens % world == 0 else None
+    del full
     hbm_peak, peak_kind = peaks()
     if rank == 0:
         flops = layer_flops(T) * world
@@ -396,17 +604,16 @@ def run_ep(args, world, rank, dev):
             "metric": METRIC, "value": T * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
-            "config": {"workload": f"K3-shape prefill MoE layer, expert parallel over {world} GPUs (config 4 layout)",
-                       "T_per_gpu": T, "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I,
-                       "rs": RS, "global_batch": T * world, "seq_len": T, "parallelism": f"ep{world}",
-                       "expert_placement": args.ep_placement, "fc2_slices": args.ep_overlap,
-                       "fc2_grid_cap": args.ep_fc2_cap,
-                       "l2": "inputs larger than L2: each GPU streams its experts' weights every step"},
+            "config": ep_config(T, E, world, args),
             "tflops": flops / (ms / 1e3) / 1e12,
             "a2a_ms": {"dispatch": disp_ms, "combine": comb_ms},
+            "ep_bit_identical": ep_identical,
+            "parity": {"ep_bit_identical": ep_identical, "ranks_checked": world,
+                       "against": "the 1-GPU layer over all experts on each rank's own 8192 rows", "ok": ep_identical},
             "roofline": {"kernel": "FC1 grouped GEMM (grouped_gemm_kernel<0>), rank 0", "bound": "hbm",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes, "traffic": None},
+                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes,
+                         "traffic": fc1_traffic(fc1_bytes), "traffic_source": TRAFFIC_SOURCE},
             "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4) * world,
                     "d2h_bytes_per_step": int(x.numel() * 2) * world,
@@ -415,6 +622,7 @@ def run_ep(args, world, rank, dev):
             # topk, 2 x 3 plan launches, pairs, pack, shared pack, ids, 3 table launches, unpack, return rows,
             # FC1, FC2 (a launch a slice), combine
             "gpu_launches": (18 + args.ep_overlap) * args.steps,
+            "decode": dec,
             "clocks": clk.summary(),
             "cpu_baseline": None,
         }
@@ -423,13 +631,87 @@ def run_ep(args, world, rank, dev):
     dist.destroy_process_group()
 
 
-# ------------------------------------------------------------------ decode (config 2): --decode
+# ------------------------------------------------------------------ decode (config 2)
 DECODE_METRIC = "EP decode us/layer (64 tokens x top-8)"
 
 
+def decode_pass(args, world, rank, dev, w, owner, full):
+    """Config 2 inside the expert-parallel run: 64 tokens (rank r owns rows [r T, r T + T) of one global batch)
+    through this rank's experts `w`, fixed-size all-to-all blocks (no host synchronisation), the whole step
+    captured as one CUDA graph and replayed.  Returns us a layer (max over ranks), an eager breakdown, and
+    whether every rank's output equals the 1-GPU layer `full` on the same rows."""
+    import torch
+    import torch.distributed as dist
+
+    import k3moe_ep
+
+    E, Tall = args.experts, args.decode_tokens
+    T = Tall // world
+    x_all, S_all, bias, rs = device_inputs(host_inputs(Tall, E, 2000), dev)
+    x, S = x_all[rank * T:(rank + 1) * T].contiguous(), S_all[rank * T:(rank + 1) * T].contiguous()
+    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
+    run = lambda: layer.forward(S, x)  # noqa: E731
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            run()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    steps = max(args.steps, 20)
+
+    def mx(v):
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(step):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        return mx(a.elapsed_time(b) / steps * 1e3)
+
+    eager_us = timed(run)
+    # eager breakdown: the dispatch all-to-all, the expert GEMMs (tables .. FC2), the combine all-to-all
+    names = ("dispatch", "ffn", "combine")
+    ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
+    dist.barrier()
+    layer.forward(S, x, ev)
+    torch.cuda.synchronize()
+    stage_us = {n: round(mx(ev[n][0].elapsed_time(ev[n][1]) * 1e3), 1) for n in names}
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = run()
+    graph.replay()
+    torch.cuda.synchronize()
+    us = timed(graph.replay)
+    graph.replay()
+    torch.cuda.synchronize()
+    ref = full.forward(S, x)
+    torch.cuda.synchronize()
+    same = torch.tensor([1 if torch.equal(static_out.view(torch.int16), ref.view(torch.int16)) else 0], device=dev)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    counts = layer.last["tables"].counts.cpu().numpy()
+    per_expert = 2 * I * H // 2 + 2 * I * H // 32 + H * I // 2 + H * I // 32
+    wbytes = mx(float(int((counts > 0).sum()) * per_expert))
+    hbm_peak, _ = peaks()
+    graph.reset()
+    del graph
+    torch.cuda.synchronize()
+    return {"us": us, "eager_us": eager_us, "graph": True, "tokens": Tall, "tokens_per_gpu": T,
+            "stage_us_eager": stage_us, "bit_identical_to_1gpu": bool(same.item() == 1),
+            "roofline": {"bound": "hbm", "bytes_slowest_rank": wbytes,
+                         "frac": wbytes / (us / 1e6) / 1e9 / hbm_peak}}
+
+
 def run_decode(args, world, rank, dev):
-    """Config 2: one MoE decode step of 64 tokens x top-8 over E = 896 experts, expert parallel over the N GPUs
-    (E/N contiguous experts each, 64/N tokens each); the figure is microseconds a layer, max over ranks."""
+    """Config 2 alone (`--decode`): one MoE decode step of 64 tokens x top-8 over E = 896 experts, expert
+    parallel over the N GPUs (64/N tokens each); the figure is microseconds a layer, max over ranks."""
     import torch
     import torch.distributed as dist
 
@@ -440,17 +722,13 @@ def run_decode(args, world, rank, dev):
     if Tall % world or E % world:
         raise SystemExit(f"--decode needs tokens ({Tall}) and experts ({E}) divisible by {world}")
     T, El = Tall // world, E // world
-    # the same 64 tokens whatever N: rank r owns rows [r T, r T + T) of one global batch
-    x_all, S_all, bias, rs = rank_inputs(Tall, E, 0, dev)
+    x_all, S_all, bias, rs = device_inputs(host_inputs(Tall, E, 2000), dev)
     x, S = x_all[rank * T:(rank + 1) * T].contiguous(), S_all[rank * T:(rank + 1) * T].contiguous()
     if world == 1:
-        w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, (E + SHARED) * 2 * I, H, WSD, device=dev)
-        w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, (E + SHARED) * H, I, WSD, device=dev)
-        layer = k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
+        layer = full_layer(E, bias, rs, T, dev)
         out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
         run = lambda: layer.forward(S, x, out)  # noqa: E731
     else:
-        # fixed-size all-to-all blocks: no host synchronisation in the step, so it can be graph-captured
         owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
         w = rank_weights(E, mine, dev)
         layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
@@ -484,24 +762,14 @@ def run_decode(args, world, rank, dev):
 
     eager_us = timed(run)
     # the whole step (its NCCL calls included) as one CUDA graph, replayed
-    graph, graph_note = None, None
-    try:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            static_out = run()
-        graph.replay()
-        torch.cuda.synchronize()
-    except Exception as ex:  # capture unsupported here: the eager step is the figure
-        graph, graph_note = None, f"graph capture failed: {type(ex).__name__}: {str(ex)[:120]}"
-    ok = torch.tensor([1.0 if graph is not None else 0.0], device=dev)
-    if world > 1:
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-    if ok.item() < 1.0:
-        graph = None
-    step = graph.replay if graph is not None else run
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = run()
+    graph.replay()
+    torch.cuda.synchronize()
     uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     with ClockSampler(uuid) as clk:
-        us = timed(step)
+        us = timed(graph.replay)
     # end to end: this rank's x and S from pinned host memory into the step's inputs, its output back
     x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
     out_h = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
@@ -513,12 +781,8 @@ def run_decode(args, world, rank, dev):
     for _ in range(n_e2e):
         x.copy_(x_h, non_blocking=True)
         S.copy_(S_h, non_blocking=True)
-        if graph is not None:
-            graph.replay()
-            o = static_out
-        else:
-            o = run()
-        out_h.copy_(o, non_blocking=True)
+        graph.replay()
+        out_h.copy_(static_out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e_us = max_over_ranks(e0.elapsed_time(e1) / n_e2e * 1e3)
@@ -550,17 +814,13 @@ def run_decode(args, world, rank, dev):
             "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
                     "d2h_bytes_per_step": int(x.numel() * 2)},
             "gpu_launches": (8 if world == 1 else 14) * args.steps,
-            "cuda_graph": graph is not None, "eager_us": eager_us,
+            "cuda_graph": True, "eager_us": eager_us,
             "clocks": clk.summary(),
             "cpu_baseline": None,
         }
-        if graph_note:
-            line["note"] = graph_note
         print(json.dumps(line), flush=True)
-    # a graph holding NCCL calls is released before the process group goes (step holds a reference too)
-    step = None
-    if graph is not None:
-        graph.reset()
+    # a graph holding NCCL calls is released before the process group goes
+    graph.reset()
     del graph
     torch.cuda.synchronize()
     if world > 1:
@@ -630,6 +890,26 @@ def run_native(args, dev):
     print(json.dumps(line), flush=True)
 
 
+TRAFFIC_SOURCE = ("ncu DRAM bytes (read + write) per algorithmic byte of FC1 on the small-case capture "
+                  "(profiles/grouped_gemm_fc1_fc2_small_case.md), times this launch's algorithmic bytes")
+
+
+def fc1_traffic(fc1_bytes):
+    """DRAM bytes (read + write) of one FC1 launch of this workload: the ratio of DRAM traffic to algorithmic
+    bytes measured by ncu on the small-case capture of the same kernel
+    (profiles/grouped_gemm_fc1_fc2_small_case.md, line "fc1_dram_per_algorithmic_byte: R"), scaled by this
+    launch's algorithmic bytes (traffic grows with the touched experts' weights and the rows, as the bytes do).
+    Returns the bytes, or None when the summary is absent."""
+    tf = os.path.join(ROOT, "profiles", "grouped_gemm_fc1_fc2_small_case.md")
+    if not os.path.exists(tf):
+        return None
+    for ln in open(tf):
+        if ln.startswith("fc1_dram_per_algorithmic_byte:"):
+            r = float(ln.split(":")[1].strip())
+            return r * fc1_bytes
+    return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -639,8 +919,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=T_DEF)
     ap.add_argument("--experts", type=int, default=896, help="routed experts (smaller only for profiling captures)")
     ap.add_argument("--e2e-steps", type=int, default=0, help="e2e steps (default: --steps)")
-    ap.add_argument("--cpu-tiles", type=int, default=8)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-tiles", type=int, default=16, help="token tiles in the CPU leg's sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU leg (parity check and baseline)")
     ap.add_argument("--decode", action="store_true", help="config 2: one 64-token decode step, us/layer")
     ap.add_argument("--decode-tokens", type=int, default=64)
     ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
@@ -684,22 +964,15 @@ def main():
     ne = E + SHARED
     w13, w13_sf = k3moe.synth_mxfp4(W_SEED13, ne * 2 * I, H, WSD, device=dev)
     w2, w2_sf = k3moe.synth_mxfp4(W_SEED2, ne * H, I, WSD, device=dev)
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
-    x = torch.randn((T, H), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    g.manual_seed(7)
-    wr = torch.randn((H, E), generator=g, device=dev, dtype=torch.float32) / H ** 0.5
-    S = (x.float() @ wr).contiguous()
-    bias = (torch.rand(E, generator=g, device=dev) * 0.2 - 0.1).float()
-    rs = torch.tensor([RS], dtype=torch.bfloat16, device=dev)
-    del wr
+    hin = host_inputs(T, E, 1000)
     zipf = None
     if args.zipf:  # config 3: bias fitted (on the host) so the realised top-8 histogram follows Zipf(1.1)
         import cases
 
-        zb, beta, kl = cases.zipf_bias(S.cpu().numpy(), K)
-        bias = torch.from_numpy(zb).to(dev)
+        zb, beta, kl = cases.zipf_bias(hin["S"], K)
+        hin["bias"] = zb
         zipf = {"s": 1.1, "seed": 3, "beta": beta, "kl": round(kl, 4)}
+    x, S, bias, rs = device_inputs(hin, dev)
     layer = k3moe.MoELayer(H, I, E, K, SHARED, w13, w13_sf, w2, w2_sf, bias, rs, max_tokens=T, device=dev)
     out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
 
@@ -716,9 +989,6 @@ def main():
             e.record(stream)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     with ClockSampler(uuid) as clk:
         start.record(stream)
@@ -726,9 +996,6 @@ def main():
             layer.forward_events(S, x, out, ev[s])
         stop.record(stream)
         torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     layer.check_device_error(T)
     ms = start.elapsed_time(stop) / args.steps
     # GEMM role counters over 2 extra (untimed) steps: where each role of FC1 / FC2 spends its cycles
@@ -755,11 +1022,7 @@ def main():
             "producer_wait_stage": round(c["producer_wait_stage"] / max(c["producer"], 1), 3),
             "epilogue_busy": round(1 - c["epilogue_wait_acc"] / max(c["epilogue"], 1), 3),
         }
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = T * world / (ms / 1e3)
+    value = T / (ms / 1e3)
 
     # ---------------- tables of the run: algorithmic bytes of FC1 (the dominant kernel)
     off = layer.offsets(T)
@@ -774,14 +1037,6 @@ def main():
     fc1_ms = float(stage_ms[3])
     hbm_peak, peak_kind = peaks()
     achieved = fc1_bytes / (fc1_ms / 1e3) / 1e9
-    # DRAM bytes (read + write) of one FC1 launch of this workload, from the ncu capture summarised in
-    # profiles/grouped_gemm_fc1_config1_traffic.md (line "bytes_per_launch: N")
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "grouped_gemm_fc1_config1_traffic.md")
-    if os.path.exists(tf) and T == T_DEF and E == 896 and not args.zipf:
-        for ln in open(tf):
-            if ln.startswith("bytes_per_launch:"):
-                traffic = int(ln.split(":")[1].strip())
 
     # ---------------- end to end through the public API: host x/S in, host out back
     e2e_steps = args.e2e_steps or args.steps
@@ -793,78 +1048,52 @@ def main():
         return od
 
     e2e_ms = e2e_overlapped(fwd, S_h, x_h, (T, H), e2e_steps, stream, dev)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
     layer.check_device_error(T)
 
-    # ---------------- CPU baseline (rank 0, N = 1): the oracle on a bounded sample
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    # ---------------- the CPU leg (after timing): the oracle checks this run's own intermediates on sampled
+    # token tiles and every row's routing, and its FC1 + FC2 time over the sample is the CPU baseline
+    cpu, parity = None, None
+    if not args.no_cpu_baseline:
         import oracle
 
-        threads = oracle.set_threads(0)
-        cb = ws[off["cta_batch"]:off["cta_batch"] + 4 * nne].view(torch.int32).cpu().numpy()
-        cl = ws[off["cta_limit"]:off["cta_limit"] + 4 * nne].view(torch.int32).cpu().numpy()
-        tb = {"cta_batch": cb, "cta_limit": cl}
+        threads = oracle.set_threads(host_threads())
+        layer.forward(S, x, out)  # the workspace holds this call's intermediates
+        torch.cuda.synchronize()
         tiles = sample_tiles_of(nne, args.cpu_tiles)
-        kg4 = H // 128
-        a13 = 2 * I * (H // 2)
-        s13 = 2 * I // 128 * kg4 * 512
-        a2 = H * (I // 2)
-        s2 = H // 128 * (I // 128) * 512
-
-        def wsrc(e):
-            return (w13[e * 2 * I:(e + 1) * 2 * I].cpu().numpy(), w13_sf[e * s13:(e + 1) * s13].cpu().numpy(),
-                    w2[e * H:(e + 1) * H].cpu().numpy(), w2_sf[e * s2:(e + 1) * s2].cpu().numpy())
-
-        qp = ws[off["q_perm"]:]
-        sfp = ws[off["sf_perm"]:]
-
-        def qsrc(c):
-            q = qp[c * 128 * H:(c + 1) * 128 * H].view(128, H).cpu().numpy()
-            sf = sfp[c * kg4 * 512:(c + 1) * kg4 * 512].cpu().numpy()
-            return q, sf
-
-        rs_bits = int(rs.view(torch.int16).item()) & 0xFFFF
-        t_topk = cpu_topk_time(S.cpu().numpy(), bias.cpu().numpy(), rs_bits)
-        t_fc = cpu_sample(tiles, tb, wsrc, qsrc, threads)
+        wd = {"w13": w13, "w13_sf": w13_sf, "w2": w2, "w2_sf": w2_sf}
+        parity, t_topk, t_fc = inrun_parity(layer, hin, wd, out, T, E, tiles)
         sec = t_topk + t_fc * nne / len(tiles)
         cpu = {"value": T / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": (f"router top-k over all {T} rows ({t_topk:.2f} s) + oracle FC1+FC2 over {len(tiles)} of "
-                          f"{nne} token tiles ({t_fc:.2f} s), scaled by {nne}/{len(tiles)}")}
+                          f"{nne} token tiles ({t_fc:.2f} s, spread evenly), projected to all {nne} tiles")}
 
-    if rank == 0:
-        flops = layer_flops(T) * world
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
-            "config": prefill_config(T, E, zipf),
-            "tflops": flops / (ms / 1e3) / 1e12,
-            "pct_fp8_peak": flops / (ms / 1e3) / 1e12 / (FP8_PEAK_TFLOPS * world) * 100,
-            "stage_ms": dict(zip(k3moe.MoELayer.STAGES, [round(float(v), 4) for v in stage_ms])),
-            "routing": {"num_non_exiting": nne, "routed_rows": routed_rows, "touched_experts": touched,
-                        "empty_experts": int((counts[:E] == 0).sum()), "max_expert_rows": int(counts[:E].max())},
-            "roofline": {"kernel": "FC1 grouped GEMM (grouped_gemm_kernel<0>)", "bound": "hbm",
-                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes,
-                         "traffic": traffic},
-            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
-                    "d2h_bytes_per_step": int(out.numel() * 2),
-                    "copies": "every step's x, S in and output back over PCIe, on side streams overlapping the "
-                              "neighbouring steps' compute (double buffers)"},
-            "gpu_launches": 8 * args.steps,
-            "gemm_trace": gemm_trace,
-            "clocks": clk.summary(),
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    flops = layer_flops(T)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "mxfp8 x mxfp4 (f32 accumulate)", "data": "synthetic",
+        "config": prefill_config(T, E, zipf),
+        "tflops": flops / (ms / 1e3) / 1e12,
+        "pct_fp8_peak": flops / (ms / 1e3) / 1e12 / FP8_PEAK_TFLOPS * 100,
+        "stage_ms": dict(zip(k3moe.MoELayer.STAGES, [round(float(v), 4) for v in stage_ms])),
+        "routing": {"num_non_exiting": nne, "routed_rows": routed_rows, "touched_experts": touched,
+                    "empty_experts": int((counts[:E] == 0).sum()), "max_expert_rows": int(counts[:E].max())},
+        "roofline": {"kernel": "FC1 grouped GEMM (grouped_gemm_kernel<0>)", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "peak_kind": peak_kind, "algorithmic_bytes_per_launch": fc1_bytes,
+                     "traffic": fc1_traffic(fc1_bytes), "traffic_source": TRAFFIC_SOURCE},
+        "parity": parity,
+        "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4),
+                "d2h_bytes_per_step": int(out.numel() * 2),
+                "copies": "every step's x, S in and output back over PCIe, on side streams overlapping the "
+                          "neighbouring steps' compute (double buffers)"},
+        "gpu_launches": 8 * args.steps,
+        "gemm_trace": gemm_trace,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -149,6 +149,19 @@ int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_pe
                   uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
                   int activation, k3moe_stream_t stream);
 
+/* The two TMA descriptors (128 bytes each: the weights', then the activations') that the module entries
+ * kern_k3_moe_fc1 / kern_k3_moe_fc2 of k3moe_module.cubin read through their `maps` argument, encoded for
+ * buffers at fixed addresses and copied to maps_dev (256 bytes of device memory, 64-byte aligned): a load-time
+ * call, once the buffers are placed; it synchronises `stream`.  mode 0: FC1 over w = W13 [n_experts*2I, H/2]
+ * and act = q_perm [cap_rows, H]; mode 1: FC2 over w = W2 [n_experts*H, I/2] and act = fc1_q [cap_rows, I].
+ * The module entries take the reference ops' parameter lists (scripts/k3_moe_bmm.py:131-134, 167-169) and
+ * replace the trtllm_bmm launches of scripts/k3_moe_bmm.py:112-113, whose 17,472-byte parameter block carries
+ * its own descriptors (docs/k3-kernel-abi.md:549-565). */
+#define K3MOE_GEMM_THREADS 384        /* block of kern_k3_moe_fc1 / kern_k3_moe_fc2 */
+#define K3MOE_GEMM_SMEM_BYTES 204032  /* their dynamic shared memory */
+int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n_experts, int H, int I, int cap_rows,
+                           void* maps_dev, k3moe_stream_t stream);
+
 /* FC2 over the output columns [col0, col0 + ncols) only (multiples of 256), stored at
  * out_bf16 + out_rows[r] * ldo (out_rows null: row r), with at most grid_cap persistent
  * blocks (0: one an SM; fewer leave SMs to a collective running beside it). */
@@ -229,6 +242,18 @@ int k3moe_combine(const void* fc2_bf16, const int32_t* exp2perm, const float* wt
  * E2M1, saturate at 6); packed [rows, K/2], scales tiled (see top).
  * No reference counterpart: the reference consumes pre-quantised checkpoints. */
 int k3moe_quant_mxfp4(const float* w, long long rows, int K, uint8_t* packed, uint8_t* sf, k3moe_stream_t stream);
+/* A checkpoint's MXFP4 expert weights into the layout above, on the device (once, at load): packed_rows
+ * [experts * rows_per_expert, K/2] E2M1 (element 2i in the low nibble) and scale_rows
+ * [experts * rows_per_expert, K/32] UE8M0, both row-major, experts back to back, as the checkpoint's
+ * `weight_packed` / `weight_scale` tensors are bound; -> packed (tile-major) and sf (128x4-tiled).
+ * gated = 1 for FC1, whose checkpoint rows come as [w3 (up); w1 (gate)]: the halves are swapped into
+ * [gate; up].  rows_per_expert and K multiples of 128; packed pointers 16-byte, scale pointers 4-byte aligned.
+ * Replaces: the load-time kern_k3_moe_w_shuffle / kern_k3_moe_sf_shuffle (source/k3_moe_prefill.cu:237-259;
+ *   scripts/k3_moe_bmm.py:176-184; bound at scripts/gen_stage.py:681-702), which lay the same bytes out
+ *   for the TRT-LLM-gen GEMMs; the module entries kern_k3_moe_w_tiles / kern_k3_moe_sf_tiles take
+ *   their parameter lists. */
+int k3moe_import_mxfp4(const uint8_t* packed_rows, const uint8_t* scale_rows, int experts, int rows_per_expert,
+                       int K, int gated, uint8_t* packed, uint8_t* sf, k3moe_stream_t stream);
 /* Synthetic weights of stream `seed` (rows [row0, row0+rows)), quantised as above. */
 int k3moe_synth_mxfp4(uint64_t seed, long long row0, long long rows, int K, float sd, uint8_t* packed, uint8_t* sf,
                       k3moe_stream_t stream);

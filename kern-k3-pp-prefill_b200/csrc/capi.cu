@@ -14,6 +14,9 @@
 
 using namespace k3;
 
+static_assert(gemm::THREADS == K3MOE_GEMM_THREADS && gemm::SMEM_BYTES == K3MOE_GEMM_SMEM_BYTES,
+              "the module GEMM entries' launch geometry in include/k3moe.h");
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -136,6 +139,8 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   p.out_bf16 = reinterpret_cast<bf16*>(out_bf16);
   p.out_rows = out_rows;
   p.act = activation;
+  p.alpha = nullptr;  // SiTU at K3's a = 4, b = 25
+  p.beta = nullptr;
   p.err = err;
   p.K = K;
   p.rows_per_expert = rows_per_expert;
@@ -327,6 +332,40 @@ int k3moe_synth_mxfp4(uint64_t seed, long long row0, long long rows, int K, floa
   const int grid = (int)std::min<long long>(cdiv(groups, 256), (long long)num_sms(current_device()) * 32);
   // the tiled scale offsets are relative to row0 (a multiple of 128): callers pass sf at row0's atom
   synth_mxfp4_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(seed, row0, rows, K, sd, packed, sf);
+  return launch_status();
+}
+
+int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n_experts, int H, int I, int cap_rows,
+                           void* maps_dev, k3moe_stream_t stream) {
+  if ((mode != 0 && mode != 1) || !w || !act || !maps_dev || n_experts < 1 || H < 256 || H % 256 || I < 256 ||
+      I % 256 || cap_rows < 128 || cap_rows % 128 || reinterpret_cast<uintptr_t>(maps_dev) % 64)
+    return K3MOE_EINVAL;
+  const int K = mode == 0 ? H : I;
+  const int rows_per_expert = mode == 0 ? 2 * I : H;
+  CUtensorMap maps[2];
+  int rc = encode_operand(&maps[0], w, (long long)n_experts * rows_per_expert, K, true);
+  if (rc) return rc;
+  rc = encode_operand(&maps[1], act, cap_rows, K, false);
+  if (rc) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(maps_dev, maps, sizeof(maps), cudaMemcpyHostToDevice, s) != cudaSuccess) return K3MOE_ELAUNCH;
+  return cudaStreamSynchronize(s) == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH;
+}
+
+int k3moe_import_mxfp4(const uint8_t* packed_rows, const uint8_t* scale_rows, int experts, int rows_per_expert,
+                       int K, int gated, uint8_t* packed, uint8_t* sf, k3moe_stream_t stream) {
+  if (experts < 1 || rows_per_expert < 128 || rows_per_expert % 128 || K < 128 || K % 128 || !packed_rows ||
+      !scale_rows || !packed || !sf || reinterpret_cast<uintptr_t>(packed_rows) % 16 ||
+      reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(scale_rows) % 4 ||
+      reinterpret_cast<uintptr_t>(sf) % 4)
+    return K3MOE_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long chunks = (long long)experts * rows_per_expert * (K / 32);  // 16-byte chunks (K/2 bytes a row)
+  const long long quads = (long long)experts * rows_per_expert * (K / 128);  // 4-byte scale pieces
+  kern_k3_moe_w_tiles<<<(unsigned)cdiv(chunks, 256), 256, 0, s>>>(packed_rows, packed, experts, rows_per_expert,
+                                                                  K / 2, gated ? 1 : 0);
+  kern_k3_moe_sf_tiles<<<(unsigned)cdiv(quads, 256), 256, 0, s>>>(scale_rows, sf, experts, rows_per_expert, K / 32,
+                                                                  gated ? 1 : 0);
   return launch_status();
 }
 

@@ -27,6 +27,7 @@ enum : u32 {
   ERR_WAIT_TIMEOUT = 1u << 0,   // an mbarrier wait ran past its time limit
   ERR_BAD_TABLE = 1u << 1,      // a routing-table entry was out of range (skipped)
   ERR_BAD_EXPERT = 1u << 2,     // a top-k id outside [0, E) reached a table kernel (skipped)
+  ERR_BAD_ARGS = 1u << 3,       // a module entry's arguments failed its checks (nothing was computed)
 };
 
 __device__ __forceinline__ void report_error(u32* err, u32 code, u32 site) {

@@ -562,6 +562,49 @@ extern "C" __global__ void kern_k3_moe_sf_shuffle(const uint8_t* __restrict__ sr
   dst[(long long)e * n * kg + sf_tiled_offset(r, c, kg / 4)] = src[((long long)e * n + gemm_row_source(r, n, gated)) * kg + c];
 }
 
+// ------------------------------------------------------------------ load-time re-layout for this build's GEMMs
+// The same inputs as the two shuffles above (the checkpoint's MXFP4 `weight_packed` rows, E2M1 two a byte with
+// element 2i in the low nibble, and their UE8M0 `weight_scale` bytes, [n rows, K/32] an expert; FC1 bound as
+// [w3 (up); w1 (gate)], scripts/gen_stage.py:681-702) and the same parameter lists, so a derive program binds
+// them by changing only the entry name; the outputs are the layout k3moe's grouped GEMMs read instead of the
+// TRT-LLM-gen one.  `gated` (FC1) swaps the halves: rows [gate (the checkpoint's second half); up (its first)].
+// Rows stay in order otherwise (the GEMMs need no epilogue permutation).  n and K multiples of 128.
+__device__ __forceinline__ int tile_row_source(int r, int n, int gated) {
+  if (!gated) return r;
+  return r < n / 2 ? r + n / 2 : r - n / 2;
+}
+
+// grid ceil(experts * n * row_bytes / 16 / block), any block: one 16-byte chunk of the output a thread.  The
+// output is tile-major (128 x 128-element tiles of 8 KB, tile (R/128, k/128) at (R/128) * (K/128) + k/128 over
+// the flattened rows R = e * n + r), so a thread's chunk is 16 bytes of one tile row.
+extern "C" __global__ void kern_k3_moe_w_tiles(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                               int experts, int n, int row_bytes, int gated) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)experts * n * (row_bytes / 16)) return;
+  const long long t = i >> 9;                  // 8 KB tile: 512 chunks
+  const int within = (int)(i & 511);
+  const int kt_n = row_bytes / 64;             // tiles along K
+  const long long R = (t / kt_n) * 128 + (within >> 2);
+  const int b = (int)(t % kt_n) * 64 + (within & 3) * 16;
+  const int e = (int)(R / n), r = (int)(R - (long long)e * n);
+  reinterpret_cast<uint4*>(dst)[i] =
+      *reinterpret_cast<const uint4*>(src + ((long long)e * n + tile_row_source(r, n, gated)) * row_bytes + b);
+}
+
+// grid ceil(experts * n * kg / 4 / block), any block: four scale bytes a thread (groups 4j..4j+3 of one row,
+// adjacent in both layouts), into the 128x4-tiled layout over the flattened rows (kg = K / 32, a multiple of 4).
+extern "C" __global__ void kern_k3_moe_sf_tiles(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                int experts, int n, int kg, int gated) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int q = kg / 4;
+  if (i >= (long long)experts * n * q) return;
+  const long long R = i / q;
+  const int c = (int)(i - R * q) * 4;
+  const int e = (int)(R / n), r = (int)(R - (long long)e * n);
+  const u32 v = *reinterpret_cast<const u32*>(src + ((long long)e * n + tile_row_source(r, n, gated)) * kg + c);
+  *reinterpret_cast<u32*>(dst + sf_tiled_offset(R, c, q)) = v;
+}
+
 // ------------------------------------------------------------------ the decode front (one launch)
 // kern_k3_moe_front (source/k3_moe_front.cu:358-471; op scripts/gen_stage.py:416-428, 1080-1087): a decode
 // step's MoE front over T <= 64 rows of the front GEMM's f32 output (F_LDS columns a row: router | latent |

@@ -84,15 +84,19 @@ struct GemmParams {
   int cap_rows;             // permuted-row capacity of the activations and the outputs
   int max_ctas;             // capacity of the CTA tables
   unsigned long long* trace;  // optional per-role cycle counters (16 a mode), or null
-  int act;                  // FC1 gate: 0 SwiGLU silu(g)*u, 1 K3's SiTU 4 tanh(g/4) sigmoid(g) * 25 tanh(u/25)
+  int act;                  // FC1 gate: 0 SwiGLU silu(g)*u, 1 K3's SiTU a tanh(g/a) sigmoid(g) * b tanh(u/b)
   int fb0;                  // FC2: the first 256-column block computed (a column slice [256 fb0, 256 (fb0 + nfb)))
+  const float* alpha;       // SiTU: per-expert a and b (f32 [n_experts]), or null for K3's a = 4, b = 25
+  const float* beta;
 };
 
-// FC1's gated activation of (gate g, up u)
-__device__ __forceinline__ float gated_act(float g, float u, int act) {
+// FC1's gated activation of (gate g, up u); SiTU with a = 4, b = 25 is K3's gate.  ra, rb are 1/a, 1/b
+// (exact for a = 4; the nearest float to 1/25 for b = 25, the same value as the literal 0.04f).
+__device__ __forceinline__ float gated_act(float g, float u, int act, float a = 4.0f, float ra = 0.25f,
+                                           float b = 25.0f, float rb = 0.04f) {
   const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
   if (act == 0) return g * sg * u;
-  return 4.0f * tanhf(0.25f * g) * sg * (25.0f * tanhf(0.04f * u));
+  return a * tanhf(ra * g) * sg * (b * tanhf(rb * u));
 }
 
 struct Unit {
@@ -119,10 +123,10 @@ __device__ __forceinline__ int weight_row(const GemmParams& p, const Unit& w, in
   return w.e * p.rows_per_expert + (p.fb0 + w.fb) * gemm::BN + h * 128;
 }
 
+// The kernel body: tmW / tmA point at the weight and activation tensor maps (kernel parameters for the C-ABI
+// launch, a global-memory descriptor buffer for the module entries of module_gemm.cu).
 template <int MODE>
-__global__ void __launch_bounds__(gemm::THREADS, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
-                        GemmParams p) {
+__device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmA, const GemmParams& p) {
   using namespace gemm;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -152,8 +156,8 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    prefetch_tmap(&tmW);
-    prefetch_tmap(&tmA);
+    prefetch_tmap(tmW);
+    prefetch_tmap(tmA);
   }
   tc_fence_before();
   __syncthreads();
@@ -192,12 +196,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           // tile-major operands: tile t = row_block * kstages + ks is rows [128 t, 128 t + 128) of the
           // maps (one contiguous chunk), and its scales are the 512-byte atom t
           const int ta = (w.row0 / BM) * kstages + ks;
-          tma_load_2d(st, &tmA, &full[stage], 0, ta * BM);
+          tma_load_2d(st, tmA, &full[stage], 0, ta * BM);
           if (!LDGSTS) bulk_load(sf, p.sfa + (long long)ta * SF_BYTES, SF_BYTES, &full[stage]);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int t = (wrow[h] / 128) * kstages + ks;
-            tma_load_2d(st + A_BYTES + h * W_TILE, &tmW, &full[stage], 0, t * 128);
+            tma_load_2d(st + A_BYTES + h * W_TILE, tmW, &full[stage], 0, t * 128);
             if (!LDGSTS) bulk_load(sf + (1 + h) * SF_BYTES, p.sfw + (long long)t * SF_BYTES, SF_BYTES, &full[stage]);
           }
           if (++stage == STAGES) {
@@ -350,6 +354,14 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
         const long long r = w.row0 + row;
         if (MODE == MODE_FC1) {
           const int kg4 = p.out_cols / 128;
+          // SiTU's a, b: per expert from the caller's buffers (the module entry), else K3's 4 and 25
+          float ga = 4.0f, gra = 0.25f, gb = 25.0f, grb = 0.04f;
+          if (p.alpha != nullptr) {
+            ga = p.alpha[w.e];
+            gb = p.beta[w.e];
+            gra = __frcp_rn(ga);
+            grb = __frcp_rn(gb);
+          }
           u32 sfw = 0;
 #pragma unroll
           for (int g = 0; g < 2; ++g) {
@@ -359,7 +371,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             for (int j = 0; j < 32; ++j) {
               const float gf = __uint_as_float(v[g][j]);
               const float uf = __uint_as_float(v[2 + g][j]);
-              hv[j] = gated_act(gf, uf, p.act);
+              hv[j] = gated_act(gf, uf, p.act, ga, gra, gb, grb);
               amax = fmaxf(amax, fabsf(hv[j]));
             }
             const int e = mx8_exponent_exact(amax);
@@ -404,6 +416,13 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(gemm::THREADS, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
+                        GemmParams p) {
+  grouped_gemm_body<MODE>(&tmW, &tmA, p);
 }
 
 }  // namespace k3

@@ -317,10 +317,9 @@ __device__ __forceinline__ uint2 quant8_lanes(const uint4 u, int& sfbyte) {
 // shared expert's row).  q in the tile-major operand layout (op8_offset), SF in
 // the 128x4-tiled layout over permuted rows.
 // One warp a row; a lane covers 8 columns of each 256-column piece.
-__global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restrict__ x, int ldx, int R, int cols, int K,
-                                                            const int* __restrict__ exp2perm,
-                                                            const int* __restrict__ meta, uint8_t* __restrict__ qp,
-                                                            uint8_t* __restrict__ sfp) {
+__device__ __forceinline__ void quant_permute_rows(const bf16* __restrict__ x, int ldx, int R, int cols, int K,
+                                                   const int* __restrict__ exp2perm, const int* __restrict__ meta,
+                                                   uint8_t* __restrict__ qp, uint8_t* __restrict__ sfp) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int kt = cols / 128, kg4 = (cols / 32 + 3) / 4;
@@ -366,6 +365,13 @@ __global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restri
       }
     }
   }
+}
+
+__global__ void __launch_bounds__(256) quant_permute_kernel(const bf16* __restrict__ x, int ldx, int R, int cols, int K,
+                                                            const int* __restrict__ exp2perm,
+                                                            const int* __restrict__ meta, uint8_t* __restrict__ qp,
+                                                            uint8_t* __restrict__ sfp) {
+  quant_permute_rows(x, ldx, R, cols, K, exp2perm, meta, qp, sfp);
 }
 
 // Linear-SF quantiser (kern_k3_moe_quant's layout): q [rows, cols], sf [rows, cols/32].

@@ -66,6 +66,8 @@ SIGNATURES = {
     "k3moe_ep_ids_k": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "k3moe_ep_unpack_k": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "k3moe_ep_return_rows": (_I, [_P, _I, _I, _P, _P]),
+    "k3moe_import_mxfp4": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
+    "k3moe_gemm_tensor_maps": (_I, [_I, _P, _P, _I, _I, _I, _I, _P, _P]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",
@@ -258,6 +260,20 @@ def quant_mxfp4(w: torch.Tensor, stream=None):
     packed = torch.empty((rows, K // 2), dtype=torch.uint8, device=w.device)
     sf = torch.zeros((-(-rows // 128)) * (K // 128) * 512, dtype=torch.uint8, device=w.device)
     _check(lib().k3moe_quant_mxfp4(_p(w), rows, K, _p(packed), _p(sf), _stream(stream)), "quant_mxfp4")
+    return packed, sf
+
+
+def import_mxfp4(packed_rows: torch.Tensor, scale_rows: torch.Tensor, experts: int, gated: bool, stream=None):
+    """A checkpoint's MXFP4 expert tensors (row-major `weight_packed` [experts*n, K/2] and `weight_scale`
+    [experts*n, K/32], FC1 as [w3 (up); w1 (gate)] with gated=True) -> (packed tile-major, scales tiled), the
+    layout the grouped GEMMs read (k3moe_import_mxfp4)."""
+    rows, half = packed_rows.shape
+    K = half * 2
+    n = rows // experts
+    packed = torch.empty((rows, half), dtype=torch.uint8, device=packed_rows.device)
+    sf = torch.empty(rows * K // 32, dtype=torch.uint8, device=packed_rows.device)
+    _check(lib().k3moe_import_mxfp4(_p(packed_rows), _p(scale_rows), experts, n, K, int(gated), _p(packed), _p(sf),
+                                    _stream(stream)), "import_mxfp4")
     return packed, sf
 
 

@@ -271,8 +271,9 @@ class EPMoELayer:
         dist.all_to_all_single(ob, ib, [r * row_bytes for r in out_rows], [r * row_bytes for r in in_rows],
                                group=self.group)
 
-    def _forward_fixed(self, S, x):
-        """forward() with fixed-size all-to-all blocks: cap = fixed_tokens * K slots a destination."""
+    def _forward_fixed(self, S, x, events=None):
+        """forward() with fixed-size all-to-all blocks: cap = fixed_tokens * K slots a destination.
+        events: optional {"dispatch", "ffn", "combine": (start, end)} CUDA events to record."""
         ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
         T = x.shape[0]
         if T > self.fixed_tokens:
@@ -294,7 +295,12 @@ class EPMoELayer:
         ops.pack(x, lid.contiguous(), slot, LOCAL_IDS, n_slots, out=send)
         R = n_slots + (T if self.shared else 0)
         recv = torch.empty((R, stride), dtype=torch.uint8, device=x.device)
+        if events:
+            events["dispatch"][0].record()
         dist.all_to_all_single(recv[:n_slots].reshape(-1), send.reshape(-1), group=self.group)
+        if events:
+            events["dispatch"][1].record()
+            events["ffn"][0].record()
         if self.shared:
             ops.pack_rows(x, El, recv[n_slots:R])
         ids = ops.ids(recv, R, H)
@@ -302,16 +308,22 @@ class EPMoELayer:
         qp, sfp = ops.unpack(recv, R, H, tb)
         y = ops.ffn(self.w, qp, sfp, tb, H, self.I, El + self.shared, R)
         back = torch.empty((n_slots, H), dtype=y.dtype, device=y.device)
+        if events:
+            events["ffn"][1].record()
+            events["combine"][0].record()
         dist.all_to_all_single(back.reshape(-1).view(torch.uint8), y[:n_slots].reshape(-1).view(torch.uint8),
                                group=self.group)
+        if events:
+            events["combine"][1].record()
         self.last = {"received_rows": None, "sent_rows": T * K, "tables": tb}
         shared_rows = y[n_slots:R] if self.shared else None
         return ops.combine(back, slot, wts, shared_rows, T, K, H)
 
     def forward(self, S, x, events=None):
-        """events: optional {"dispatch", "fc1", "combine": (start, end)} CUDA events to record."""
+        """events: optional {"dispatch", "fc1", "combine": (start, end)} CUDA events to record (fixed-block
+        mode: "dispatch", "ffn", "combine")."""
         if self.fixed_tokens is not None:
-            return self._forward_fixed(S, x)
+            return self._forward_fixed(S, x, events)
         ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
         T = x.shape[0]
         idx, wts = ops.topk(S, self.bias, self.rs, K)
