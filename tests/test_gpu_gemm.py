@@ -3,9 +3,11 @@ CPU fp32 dequantise-and-matmul oracle, through the C ABI.
 
 Tolerances: relative L2 <= 1e-2 and, per element, max(2e-2, 3 bf16 ulp + 1e-3)
 (the contract's max-abs, widened to the reference harness's element bound
-where one bf16 step of a large output exceeds 2e-2; see cases.within_contract).  The FC1 output is MXFP8, so it is compared after dequantising;
-a requantised element may land one E4M3 step away where the two sides' f32
-accumulations straddle a rounding boundary."""
+where one bf16 step of a large output exceeds 2e-2; see cases.within_contract).  The FC1 output is MXFP8, so it
+is compared after dequantising, at rel-L2 <= 1e-2 with at most 1e-4 of its E4M3 bytes differing: a requantised
+element may land one E4M3 step away where the two sides' f32 accumulations straddle a rounding boundary (one
+step of a value near 2 is 0.25, above the contract's 2e-2 max-abs, so that bound applies to FC2 and the layer
+output).  Measured on B200: bit-identical at H <= 2048; at H = 7168 1.3e-6 of the bytes differ (rel-L2 1e-4)."""
 import numpy as np
 import pytest
 import torch
@@ -55,7 +57,9 @@ def test_fc1_fc2_against_oracle(dev, cfg):
     got = oracle.dequant_rows(f1q.cpu().numpy(), f1sf.cpu().numpy(), rows)
     ref = oracle.dequant_rows(ref_q, ref_sf, rows)
     rel = cases.rel_l2(got, ref)
-    assert rel <= 2e-2, f"fc1 rel-L2 {rel:.3e}"
+    assert rel <= 1e-2, f"fc1 rel-L2 {rel:.3e}"
+    diff = np.mean(oracle.t128_rows(f1q.cpu().numpy(), rows, c.I) != oracle.t128_rows(ref_q, rows, c.I))
+    assert diff <= 1e-4, f"fc1: {diff:.2e} of the E4M3 bytes differ"
     # FC2 from the device's own FC1 output, against the oracle's FC2 of those same bytes
     y = k3moe.fc2(g["w2"], g["w2_sf"], f1q, f1sf, t, c.H, c.I, ne, err)
     torch.cuda.synchronize()
@@ -93,13 +97,13 @@ def test_fc1_fc2_tile_shapes(dev, shared):
     ref_q, ref_sf = oracle.fc1(c.w13, c.w13_sf, qp, sfp, tb["cta_batch"], tb["cta_limit"], 0, nne, c.H, c.I)
     got = oracle.dequant_rows(f1q.cpu().numpy(), f1sf.cpu().numpy(), rows)
     ref = oracle.dequant_rows(ref_q, ref_sf, rows)
-    assert cases.rel_l2(got, ref) <= 2e-2
+    assert cases.rel_l2(got, ref) <= 1e-2
     # per tile, so a wrong tile shows which size broke
     for cidx in range(nne):
         r = np.arange(cidx * 128, int(tb["cta_limit"][cidx]))
         rel = cases.rel_l2(oracle.dequant_rows(f1q.cpu().numpy(), f1sf.cpu().numpy(), r),
                            oracle.dequant_rows(ref_q, ref_sf, r))
-        assert rel <= 2e-2, f"fc1 tile {cidx} ({len(r)} rows) rel-L2 {rel:.3e}"
+        assert rel <= 1e-2, f"fc1 tile {cidx} ({len(r)} rows) rel-L2 {rel:.3e}"
     ref_y = oracle.fc2(c.w2, c.w2_sf, f1q.cpu().numpy(), f1sf.cpu().numpy(), tb["cta_batch"], tb["cta_limit"], 0, nne,
                        c.H, c.I)
     ok, rel, ratio = cases.within_contract(y.float().cpu().numpy()[rows], oracle.bf16_to_f32(ref_y[rows]))

@@ -140,7 +140,11 @@ def test_module_quant_permute_equal_c_abi(dev, T, H, E, K, shared):
     x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
     idx, _ = k3moe.route_topk(S, bias, rs, K)
     tb = k3moe.route_tables(idx, E, 0, shared)
-    qp, sfp = k3moe.quant_permute(x, tb)
+    qp = torch.zeros((tb.cap_rows, H), dtype=torch.uint8, device=dev)
+    sfp = torch.zeros(tb.cap_rows * H // 32, dtype=torch.uint8, device=dev)
+    rc = k3moe.lib().k3moe_quant_permute(x.data_ptr(), H, T, H, K, tb.exp2perm.data_ptr(), tb.meta.data_ptr(),
+                                         qp.data_ptr(), sfp.data_ptr(), k3moe._stream())
+    assert rc == 0
     oq = torch.zeros_like(qp)
     osf = torch.zeros_like(sfp)
     rk.launch(rk.function(MOD, "kern_k3_moe_quant_permute"), (148, 1, 1), (256, 1, 1),
