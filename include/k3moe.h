@@ -229,6 +229,47 @@ int k3moe_combine_ep_chunked(const void* back_bf16, long long back_chunk_stride,
                              const float* wts, const void* shared_bf16, long long shared_chunk_stride, int ld_shared,
                              void* out_bf16, int ldo, int T, int K, int cols, int chunk_cols, k3moe_stream_t stream);
 
+/* ---------------------------------------------------------------- expert parallelism over peer memory
+ * The same exchange without the two all-to-all passes: the pack kernel stores each row straight into the
+ * destination rank's receive buffer, and FC2's epilogue stores each result row straight into the owner's
+ * return buffer, over NVLink through CUDA IPC mappings; then a flag a (source rank, phase) tells the receiver
+ * that a source's stores are complete.  The owner's combine (k3moe_combine_ep) reads only local memory: the
+ * combine is folded into the collective's receive side.  W <= 16 ranks.
+ * Replaces the combine fused with the collective of the reference's decode step (kern_k3_ar_finalize_rms,
+ * source/k3_ar_fused.cu:916, a Lamport all-reduce over peer memory; its spin waits end in __trap, these end
+ * in an error word). */
+/* k3moe_ep_pack_pairs with rank d's slot p at row_base[d] + p * stride (row_base: host array of W device
+ * addresses, 16-byte aligned; a peer's receive buffer shifted by the slots of lower ranks). */
+int k3moe_ep_pack_pairs_to(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* dest, const int32_t* lid,
+                           const int32_t* pair_pos, int W, const uint64_t* row_base, int stride,
+                           k3moe_stream_t stream);
+/* row_ptrs[perm[i*K + j]] = the address of the (i, j) pair's result row: with q = out_rows[perm] in block s
+ * ([block_start[s], block_start[s+1]), s < nblocks), block_base[s] + (q - block_start[s]) * row_bytes
+ * (host arrays; bases 32-byte aligned).  A q in no block is recorded in err (site 0xB00) and sent to `sink`
+ * (a local row of row_bytes). */
+int k3moe_ep_row_ptrs(const int32_t* perm, int R, int K, const int32_t* out_rows, int nblocks,
+                      const uint64_t* block_base, const int64_t* block_start, int64_t row_bytes, void* sink,
+                      uint64_t* row_ptrs, uint32_t* err, k3moe_stream_t stream);
+/* FC2 storing permuted row r at the device address row_ptrs[r] (a row of H bf16 columns, 32-byte aligned,
+ * in this GPU's memory or a peer's). */
+int k3moe_fc2_to_ptrs(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+                      const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const uint64_t* row_ptrs,
+                      int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream);
+/* After this stream's earlier stores: epoch into slot slot0 + me of every other rank's flag array
+ * (flag_bases: host array of W device addresses of u32 flag arrays, peers' through IPC). */
+int k3moe_ep_signal(const uint64_t* flag_bases, int W, int me, int slot0, uint32_t epoch, k3moe_stream_t stream);
+/* Wait on the device until flags[s] >= epoch (serial-number order) for every s < W but `skip`, at most
+ * budget_ns: a source still late then is recorded in err (K3MOE_EDEVICE from k3moe_read_error: bit 0, site
+ * 0xA00 + s) and the wait returns; later work on the stream runs (the caller checks err). */
+int k3moe_ep_wait(const uint32_t* flags, int W, int skip, uint32_t epoch, uint64_t budget_ns, uint32_t* err,
+                  k3moe_stream_t stream);
+/* CUDA IPC of a buffer inside any device allocation: a 64-byte handle of the allocation holding dev_ptr and
+ * dev_ptr's offset in it; import maps a peer's handle into this process (peer access enabled) and returns
+ * the buffer's address; release unmaps it. */
+int k3moe_ipc_export(const void* dev_ptr, void* handle64, uint64_t* offset);
+int k3moe_ipc_import(const void* handle64, uint64_t offset, void** dev_ptr);
+int k3moe_ipc_release(void* dev_ptr, uint64_t offset);
+
 /* ---------------------------------------------------------------- combine
  * out[t] = bf16( sum over k = 0..K-1 with exp2perm >= 0 of fma(wts, fc2[p], acc)
  * in f32, k in order, then + fc2[meta[2] + t] when meta and meta[2] >= 0 );

@@ -10,6 +10,7 @@
 #include "gemm.cu"
 #include "route.cu"
 #include "ep.cu"
+#include "ep_peer.cu"
 #include "dropin.cu"
 
 using namespace k3;
@@ -85,6 +86,22 @@ int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool
   return r == CUDA_SUCCESS ? K3MOE_OK : K3MOE_ETMAP;
 }
 
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+// cuMemGetAddressRange: the base of the allocation holding a pointer (an IPC handle names a whole allocation)
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
+  });
+  return fn;
+}
+
 unsigned long long* g_trace = nullptr;  // k3moe_set_trace
 
 int launch_status() { return cudaGetLastError() == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH; }
@@ -106,7 +123,7 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
                 const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, uint8_t* out_q,
                 uint8_t* out_sf, void* out_bf16, int H, int I, int n_experts, int cap_rows, int max_ctas,
                 uint32_t* err, cudaStream_t stream, const int32_t* out_rows = nullptr, int activation = 0,
-                int col0 = 0, int ncols = 0, int ldo = 0, int grid_cap = 0) {
+                int col0 = 0, int ncols = 0, int ldo = 0, int grid_cap = 0, const uint64_t* out_ptrs = nullptr) {
   if (activation != 0 && activation != 1) return K3MOE_EINVAL;
   if (ncols == 0) {
     ncols = H;
@@ -119,7 +136,7 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
       (long long)max_ctas * 128 > cap_rows)
     return K3MOE_EINVAL;
   // the epilogues store 32 bytes at a time (256-bit stores): the outputs must start 32-byte aligned
-  const void* out0 = mode == MODE_FC1 ? static_cast<const void*>(out_q) : out_bf16;
+  const void* out0 = mode == MODE_FC1 ? static_cast<const void*>(out_q) : out_ptrs ? out_ptrs : out_bf16;
   if (out0 == nullptr || reinterpret_cast<uintptr_t>(out0) % 32 != 0) return K3MOE_EINVAL;
   const int K = mode == MODE_FC1 ? H : I;
   const int rows_per_expert = mode == MODE_FC1 ? 2 * I : H;
@@ -141,6 +158,7 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   p.act = activation;
   p.alpha = nullptr;  // SiTU at K3's a = 4, b = 25
   p.beta = nullptr;
+  p.out_ptrs = reinterpret_cast<const unsigned long long*>(out_ptrs);
   p.err = err;
   p.K = K;
   p.rows_per_expert = rows_per_expert;
@@ -439,6 +457,15 @@ int k3moe_fc2_to_rows(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc
                      n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream), out_rows);
 }
 
+int k3moe_fc2_to_ptrs(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
+                      const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const uint64_t* row_ptrs,
+                      int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err, k3moe_stream_t stream) {
+  if (!row_ptrs) return K3MOE_EINVAL;
+  return gemm_launch(MODE_FC2, w2, w2_sf, fc1_q, fc1_sf, cta_batch, cta_limit, meta, nullptr, nullptr, nullptr, H, I,
+                     n_experts, cap_rows, max_ctas, err, reinterpret_cast<cudaStream_t>(stream), nullptr, 0, 0, 0, 0, 0,
+                     row_ptrs);
+}
+
 int k3moe_fc2_cols(const uint8_t* w2, const uint8_t* w2_sf, const uint8_t* fc1_q, const uint8_t* fc1_sf,
                    const int32_t* cta_batch, const int32_t* cta_limit, const int32_t* meta, const int32_t* out_rows,
                    void* out_bf16, int ldo, int col0, int ncols, int H, int I, int n_experts, int cap_rows,
@@ -506,7 +533,69 @@ int k3moe_ep_pack_pairs(const void* x_bf16, int ldx, int T, int H, int K, const 
   const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
   const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
   ep_pack_pairs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, fixed_eid, dst, stride, split);
+      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, fixed_eid, dst, stride, split,
+      EpBases{}, 0);
+  return launch_status();
+}
+
+int k3moe_ep_pack_pairs_to(const void* x_bf16, int ldx, int T, int H, int K, const int32_t* dest, const int32_t* lid,
+                           const int32_t* pair_pos, int W, const uint64_t* row_base, int stride,
+                           k3moe_stream_t stream) {
+  if (T < 0 || H <= 0 || H % 256 || ldx < H || ldx % 8 || K < 1 || K > 16 || !dest || !lid || !pair_pos ||
+      !row_base || W < 1 || W > EP_MAX_RANKS || stride < k3moe_ep_pair_row_stride(H, K) || stride % 16)
+    return K3MOE_EINVAL;
+  if (T == 0) return K3MOE_OK;
+  EpBases b{};
+  for (int d = 0; d < W; ++d) {
+    if (row_base[d] % 16) return K3MOE_EINVAL;
+    b.base[d] = row_base[d];
+  }
+  const int sms = num_sms(current_device());
+  const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
+  const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
+  ep_pack_pairs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, 0, nullptr, stride, split, b, 1);
+  return launch_status();
+}
+
+int k3moe_ep_row_ptrs(const int32_t* perm, int R, int K, const int32_t* out_rows, int nblocks,
+                      const uint64_t* block_base, const int64_t* block_start, int64_t row_bytes, void* sink,
+                      uint64_t* row_ptrs, uint32_t* err, k3moe_stream_t stream) {
+  if (R < 0 || K < 1 || K > 16 || !perm || !out_rows || !row_ptrs || !sink || nblocks < 1 ||
+      nblocks > EP_MAX_RANKS + 1 || !block_base || !block_start || row_bytes <= 0 || row_bytes % 32)
+    return K3MOE_EINVAL;
+  if (R == 0) return K3MOE_OK;
+  EpBases b{};
+  for (int s = 0; s < nblocks; ++s) {
+    if (block_base[s] % 32 || block_start[s + 1] < block_start[s]) return K3MOE_EINVAL;
+    b.base[s] = block_base[s];
+    b.start[s] = block_start[s];
+  }
+  b.start[nblocks] = block_start[nblocks];
+  const long long n = (long long)R * K;
+  const int grid = (int)std::min<long long>(cdiv(n, 256), (long long)num_sms(current_device()) * 8);
+  ep_row_ptrs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      perm, n, nblocks, out_rows, b, row_bytes, reinterpret_cast<unsigned long long>(sink),
+      reinterpret_cast<unsigned long long*>(row_ptrs), err);
+  return launch_status();
+}
+
+int k3moe_ep_signal(const uint64_t* flag_bases, int W, int me, int slot0, uint32_t epoch, k3moe_stream_t stream) {
+  if (!flag_bases || W < 1 || W > EP_MAX_RANKS || me < 0 || me >= W || slot0 < 0) return K3MOE_EINVAL;
+  EpBases b{};
+  for (int s = 0; s < W; ++s) {
+    if (s != me && (flag_bases[s] == 0 || flag_bases[s] % 4)) return K3MOE_EINVAL;
+    b.base[s] = flag_bases[s];
+  }
+  ep_signal_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(b, W, me, slot0, epoch);
+  return launch_status();
+}
+
+int k3moe_ep_wait(const uint32_t* flags, int W, int skip, uint32_t epoch, uint64_t budget_ns, uint32_t* err,
+                  k3moe_stream_t stream) {
+  if (!flags || W < 1 || W > 32 || budget_ns == 0) return K3MOE_EINVAL;
+  ep_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, W, skip, epoch,
+                                                                        (unsigned long long)budget_ns, err);
   return launch_status();
 }
 
@@ -562,6 +651,36 @@ int k3moe_combine_ep_chunked(const void* back_bf16, long long back_chunk_stride,
       reinterpret_cast<bf16*>(out_bf16), ldo, T, K, cols, chunk_cols, back_chunk_stride, back_ld,
       shared_chunk_stride);
   return launch_status();
+}
+
+int k3moe_ipc_export(const void* dev_ptr, void* handle64, uint64_t* offset) {
+  if (!dev_ptr || !handle64 || !offset) return K3MOE_EINVAL;
+  AddressRangeFn range = address_range_fn();
+  if (!range) return K3MOE_EDRIVER;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return K3MOE_EINVAL;
+  cudaIpcMemHandle_t h;
+  static_assert(sizeof(h) == 64, "a CUDA IPC handle is 64 bytes");
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return K3MOE_ELAUNCH;
+  std::memcpy(handle64, &h, sizeof(h));
+  *offset = (uint64_t)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return K3MOE_OK;
+}
+
+int k3moe_ipc_import(const void* handle64, uint64_t offset, void** dev_ptr) {
+  if (!handle64 || !dev_ptr) return K3MOE_EINVAL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return K3MOE_ELAUNCH;
+  *dev_ptr = static_cast<char*>(p) + offset;
+  return K3MOE_OK;
+}
+
+int k3moe_ipc_release(void* dev_ptr, uint64_t offset) {
+  if (!dev_ptr) return K3MOE_EINVAL;
+  return cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset) == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH;
 }
 
 int k3moe_set_trace(uint64_t* counters) {

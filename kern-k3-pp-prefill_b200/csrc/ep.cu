@@ -16,9 +16,18 @@
 //   [H + H/32, +2K)   the local expert ids (int16) of the token's picks on that rank, in pick order, -1 after
 // The receiver routes each row to all its experts; FC2's results go back one row a pick, in (token, pick)
 // order, so the owner's combine is unchanged.
+#pragma once
 #include "common.cuh"
 
 namespace k3 {
+
+constexpr int EP_MAX_RANKS = 16;
+
+// 64-bit bases a rank (or a block of rows), passed by value: the peer-memory transport's destinations.
+struct EpBases {
+  unsigned long long base[EP_MAX_RANKS + 1];
+  long long start[EP_MAX_RANKS + 2];  // row-number ranges [start[s], start[s+1]) of block s
+};
 
 // pair_ids[t*W + d] = d when token t has a pick on rank d, else -1 (W <= 64)
 __global__ void __launch_bounds__(256) ep_pairs_kernel(const int* __restrict__ dest, int T, int K, int W,
@@ -35,11 +44,13 @@ __global__ void __launch_bounds__(256) ep_pairs_kernel(const int* __restrict__ d
 
 // `split` warps a source row: quantise token t once and write it to the slot pair_pos[t*W + d] of every rank d
 // it goes to, headed by the local ids of its picks there (lid[t*K + k] where dest[t*K + k] == d, in k order);
-// with pair_pos null, slot t headed by `fixed_eid` alone.
+// with pair_pos null, slot t headed by `fixed_eid` alone.  Slot p of rank d is row p of dst, or with
+// use_bases, the row at bases.base[d] + p * stride (rank d's receive buffer, possibly in another GPU's memory).
 __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restrict__ x, int ldx, int T, int H, int K,
                                                             const int* __restrict__ dest, const int* __restrict__ lid,
                                                             const int* __restrict__ pair_pos, int W, int fixed_eid,
-                                                            uint8_t* __restrict__ dst, int stride, int split) {
+                                                            uint8_t* __restrict__ dst, int stride, int split,
+                                                            EpBases bases, int use_bases) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int pieces = H / 256, share = (pieces + split - 1) / split;
@@ -65,14 +76,16 @@ __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restri
       sfw |= __shfl_down_sync(0xffffffffu, sfw, 4);
       sfw |= __shfl_down_sync(0xffffffffu, sfw, 8);
       for (unsigned m = live; m; m &= m - 1) {
-        const long long pd = __shfl_sync(0xffffffffu, my_pos, __ffs(m) - 1);
-        uint8_t* row = dst + pd * stride;
+        const int d = __ffs(m) - 1;
+        const long long pd = __shfl_sync(0xffffffffu, my_pos, d);
+        uint8_t* row = (use_bases ? reinterpret_cast<uint8_t*>(bases.base[d]) : dst) + pd * stride;
         *reinterpret_cast<uint2*>(row + c) = w;
         if ((lane & 15) == 0) *reinterpret_cast<u32*>(row + H + kb) = sfw;
       }
     }
     if (part == 0 && my_pos >= 0) {  // lane d writes its rank's id list
-      short* ids = reinterpret_cast<short*>(dst + my_pos * stride + H + H / 32);
+      uint8_t* row = (use_bases ? reinterpret_cast<uint8_t*>(bases.base[lane]) : dst) + my_pos * stride;
+      short* ids = reinterpret_cast<short*>(row + H + H / 32);
       int n = 0;
       if (pair_pos == nullptr) {
         ids[n++] = (short)fixed_eid;

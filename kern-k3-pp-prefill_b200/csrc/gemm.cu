@@ -29,6 +29,7 @@
 // stores, so the next unit's MMAs overlap the math and the stores.  A 4-stage
 // mbarrier ring carries K blocks of 128; every wait is bounded and reports
 // instead of hanging.
+#pragma once
 #include "common.cuh"
 
 namespace k3 {
@@ -88,6 +89,8 @@ struct GemmParams {
   int fb0;                  // FC2: the first 256-column block computed (a column slice [256 fb0, 256 (fb0 + nfb)))
   const float* alpha;       // SiTU: per-expert a and b (f32 [n_experts]), or null for K3's a = 4, b = 25
   const float* beta;
+  const unsigned long long* out_ptrs;  // FC2: permuted row r is stored at the address out_ptrs[r] (a row of H
+                                       // columns, possibly another GPU's memory), or null (out_rows / out_bf16)
 };
 
 // FC1's gated activation of (gate g, up u); SiTU with a = 4, b = 25 is K3's gate.  ra, rb are 1/a, 1/b
@@ -389,8 +392,13 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
           const int kb = (w.fb * 128 + 64 * half) / 32;
           *reinterpret_cast<unsigned short*>(p.out_sf + sf_tiled_offset(r, kb, kg4)) = (unsigned short)sfw;
         } else {
-          const long long ro = p.out_rows ? (long long)p.out_rows[r] : r;
-          bf16* dst = p.out_bf16 + ro * p.out_cols + w.fb * BN + 128 * half;
+          bf16* dst;
+          if (p.out_ptrs != nullptr) {
+            dst = reinterpret_cast<bf16*>(p.out_ptrs[r]) + (p.fb0 + w.fb) * BN + 128 * half;
+          } else {
+            const long long ro = p.out_rows ? (long long)p.out_rows[r] : r;
+            dst = p.out_bf16 + ro * p.out_cols + w.fb * BN + 128 * half;
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
 #pragma unroll

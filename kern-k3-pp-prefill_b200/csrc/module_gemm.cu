@@ -93,6 +93,7 @@ extern "C" __global__ void __launch_bounds__(k3::gemm::THREADS, 1) kern_k3_moe_f
   p.fb0 = 0;
   p.alpha = act == 1 ? alpha : nullptr;
   p.beta = act == 1 ? beta : nullptr;
+  p.out_ptrs = nullptr;
   grouped_gemm_body<MODE_FC1>(maps, maps + 1, p);
 }
 
@@ -134,5 +135,6 @@ extern "C" __global__ void __launch_bounds__(k3::gemm::THREADS, 1) kern_k3_moe_f
   p.fb0 = 0;
   p.alpha = nullptr;
   p.beta = nullptr;
+  p.out_ptrs = nullptr;
   grouped_gemm_body<MODE_FC2>(maps, maps + 1, p);
 }

@@ -68,6 +68,14 @@ SIGNATURES = {
     "k3moe_ep_return_rows": (_I, [_P, _I, _I, _P, _P]),
     "k3moe_import_mxfp4": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "k3moe_gemm_tensor_maps": (_I, [_I, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "k3moe_ep_pack_pairs_to": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
+    "k3moe_ep_row_ptrs": (_I, [_P, _I, _I, _P, _I, _P, _P, ctypes.c_int64, _P, _P, _P, _P]),
+    "k3moe_fc2_to_ptrs": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "k3moe_ep_signal": (_I, [_P, _I, _I, _I, ctypes.c_uint32, _P]),
+    "k3moe_ep_wait": (_I, [_P, _I, _I, ctypes.c_uint32, _U64, _P, _P]),
+    "k3moe_ipc_export": (_I, [_P, _P, _P]),
+    "k3moe_ipc_import": (_I, [_P, _U64, _P]),
+    "k3moe_ipc_release": (_I, [_P, _U64]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",

@@ -32,6 +32,7 @@ the benchmark configurations.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -184,6 +185,44 @@ class GpuOps:
             tb.cap_rows, tb.max_ctas, self.err.data_ptr(), k3moe._stream()), "fc2_to_rows")
         return y
 
+    # ---- the peer-memory transport (k3moe_ep_pack_pairs_to / _row_ptrs / fc2_to_ptrs / _signal / _wait)
+    def pack_pairs_to(self, x, dest, lid, pair_pos, W, row_base, stride):
+        H, K = x.shape[1], dest.shape[1]
+        rb = (ctypes.c_uint64 * W)(*row_base)
+        k3moe._check(k3moe.lib().k3moe_ep_pack_pairs_to(x.data_ptr(), x.stride(0), x.shape[0], H, K, dest.data_ptr(),
+                                                        lid.data_ptr(), pair_pos.data_ptr(), W,
+                                                        ctypes.cast(rb, ctypes.c_void_p), stride, k3moe._stream()),
+                     "ep_pack_pairs_to")
+
+    def row_ptrs(self, tb, R, K, out_rows, block_base, block_start, row_bytes, sink):
+        ptrs = torch.empty(tb.cap_rows, dtype=torch.int64, device=out_rows.device)
+        nb = len(block_base)
+        bb = (ctypes.c_uint64 * nb)(*block_base)
+        bs = (ctypes.c_int64 * (nb + 1))(*block_start)
+        k3moe._check(k3moe.lib().k3moe_ep_row_ptrs(tb.exp2perm.data_ptr(), R, K, out_rows.data_ptr(), nb,
+                                                   ctypes.cast(bb, ctypes.c_void_p), ctypes.cast(bs, ctypes.c_void_p),
+                                                   row_bytes, sink.data_ptr(), ptrs.data_ptr(), self.err.data_ptr(),
+                                                   k3moe._stream()), "ep_row_ptrs")
+        return ptrs
+
+    def fc1_only(self, w, qp, sfp, tb, H, I, n_experts):
+        return k3moe.fc1(w["w13"], w["w13_sf"], qp, sfp, tb, H, I, n_experts, self.err)
+
+    def fc2_to_ptrs(self, w, f1q, f1sf, tb, H, I, n_experts, ptrs):
+        k3moe._check(k3moe.lib().k3moe_fc2_to_ptrs(
+            w["w2"].data_ptr(), w["w2_sf"].data_ptr(), f1q.data_ptr(), f1sf.data_ptr(), tb.cta_batch.data_ptr(),
+            tb.cta_limit.data_ptr(), tb.meta.data_ptr(), ptrs.data_ptr(), H, I, n_experts, tb.cap_rows, tb.max_ctas,
+            self.err.data_ptr(), k3moe._stream()), "fc2_to_ptrs")
+
+    def signal(self, flag_bases, W, me, slot0, epoch):
+        fb = (ctypes.c_uint64 * W)(*flag_bases)
+        k3moe._check(k3moe.lib().k3moe_ep_signal(ctypes.cast(fb, ctypes.c_void_p), W, me, slot0, epoch,
+                                                 k3moe._stream()), "ep_signal")
+
+    def wait(self, flags, W, skip, epoch, budget_ns):
+        k3moe._check(k3moe.lib().k3moe_ep_wait(flags.data_ptr(), W, skip, epoch, budget_ns, self.err.data_ptr(),
+                                               k3moe._stream()), "ep_wait")
+
     def combine(self, back, send_pos, wts, shared_rows, T, K, H):
         out = torch.empty((T, H), dtype=torch.bfloat16, device=back.device)
         sp = shared_rows.data_ptr() if shared_rows is not None else None
@@ -208,6 +247,79 @@ def balanced_owner(bias, world):
     return owner
 
 
+def peer_offsets(C, me):
+    """Where the peer-memory transport stores rows, for rank `me`, from C [W, W, 2] (C[s, d] = rows and picks
+    rank s sends to rank d; every rank holds the same C).  The stores reproduce the two all-to-alls' layouts:
+    received rows grouped by source rank, results returned grouped by the rank that computed them.
+    - dispatch: my pair-plan slots for rank d start at sum_{d' < d} C[me, d'].rows and land in rank d's receive
+      buffer from row sum_{s < me} C[s, d].rows: shift[d] = landing row - slot (slot p goes to row p + shift[d]);
+    - I receive R_recv = sum_s C[s, me].rows rows and P_recv = sum_s C[s, me].picks picks (source s's from
+      row sum_{s' < s}); my FC2 result q of source s (q in [pstart[s], pstart[s + 1])) goes to row
+      back_row0[s] + (q - pstart[s]) of s's return buffer, back_row0[s] = sum_{d < me} C[s, d].picks;
+    - recv_rows[d] / back_rows[d]: the rows rank d receives / gets back in all (capacity checks)."""
+    C = [[(int(C[s][d][0]), int(C[s][d][1])) for d in range(len(C))] for s in range(len(C))]
+    W = len(C)
+    shift = []
+    slot0 = 0
+    for d in range(W):
+        land = sum(C[s][d][0] for s in range(me))
+        shift.append(land - slot0)
+        slot0 += C[me][d][0]
+    pstart = [0]
+    for s in range(W):
+        pstart.append(pstart[-1] + C[s][me][1])
+    back_row0 = [sum(C[s][d][1] for d in range(me)) for s in range(W)]
+    return {"shift": shift, "R_recv": sum(C[s][me][0] for s in range(W)), "P_recv": pstart[-1], "pstart": pstart,
+            "back_row0": back_row0, "recv_rows": [sum(C[s][d][0] for s in range(W)) for d in range(W)],
+            "back_rows": [sum(C[s][d][1] for d in range(W)) for s in range(W)]}
+
+
+class PeerBuffers:
+    """One rank's memory that its peers store into, mapped into every rank (CUDA IPC): the receive buffer of
+    dispatched rows, the return buffer of FC2 results for this rank's picks, and 2W flag words (dispatch,
+    combine).  One allocation a rank, exported once; every rank imports its peers' at set-up."""
+
+    def __init__(self, W, rank, cap_rows, stride, back_rows, H, device, group=None):
+        self.W, self.rank, self.stride, self.H = W, rank, stride, H
+        self.cap_rows, self.back_cap = cap_rows, back_rows
+        recv_bytes = cap_rows * stride
+        self.back_off = -(-recv_bytes // 256) * 256
+        self.flag_off = self.back_off + -(-(back_rows * H * 2) // 256) * 256
+        total = self.flag_off + 256
+        self.mem = torch.zeros(total, dtype=torch.uint8, device=device)
+        self.recv = self.mem[:recv_bytes].view(cap_rows, stride)
+        self.back = self.mem[self.back_off:self.back_off + back_rows * H * 2].view(torch.bfloat16).view(back_rows, H)
+        self.flags = self.mem[self.flag_off:self.flag_off + 8 * W].view(torch.int32)
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_uint64()
+        k3moe._check(k3moe.lib().k3moe_ipc_export(self.mem.data_ptr(), ctypes.cast(handle, ctypes.c_void_p),
+                                                  ctypes.byref(off)), "ipc_export")
+        torch.cuda.synchronize(device)
+        mine = (bytes(handle), int(off.value))
+        every = [None] * W
+        dist.all_gather_object(every, mine, group=group)
+        self.base = []   # every rank's allocation in this process's address space
+        self._opened = []
+        for s, (h, o) in enumerate(every):
+            if s == rank:
+                self.base.append(self.mem.data_ptr())
+                continue
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            p = ctypes.c_void_p()
+            k3moe._check(k3moe.lib().k3moe_ipc_import(ctypes.cast(hb, ctypes.c_void_p), o, ctypes.byref(p)),
+                         "ipc_import")
+            self.base.append(int(p.value))
+            self._opened.append((int(p.value), o))
+        self.recv_addr = self.base
+        self.back_addr = [b + self.back_off for b in self.base]
+        self.flag_addr = [b + self.flag_off for b in self.base]
+
+    def close(self):
+        for p, o in self._opened:
+            k3moe.lib().k3moe_ipc_release(ctypes.c_void_p(p), o)
+        self._opened = []
+
+
 class EPMoELayer:
     """One rank's part of an expert-parallel MoE layer.
 
@@ -216,7 +328,8 @@ class EPMoELayer:
     """
 
     def __init__(self, H, I, E, K, shared, w, bias, rs, group=None, ops=None, device=None, fixed_tokens=None,
-                 owner=None, overlap_chunks=1, fc2_grid_cap=0):
+                 owner=None, overlap_chunks=1, fc2_grid_cap=0, transport="nccl", max_tokens=None,
+                 wait_budget_ns=5_000_000_000):
         """fixed_tokens: when set (at most that many tokens a call), every rank sends fixed-size blocks of
         fixed_tokens*K slots to every rank, empty slots marked by local expert id -1: no host
         synchronisation, so a whole step can be captured in a CUDA graph (decode-sized batches).
@@ -224,7 +337,18 @@ class EPMoELayer:
         are its local experts 0, 1, ...; `w` holds them in that order).  None: contiguous blocks.
         overlap_chunks: C > 1 splits FC2 into C column slices (H / C a multiple of 256) and returns each slice's
         results with its own all-to-all on a side stream while the next slice computes; fc2_grid_cap then
-        bounds FC2's persistent blocks (0: one an SM) to leave SMs to the collective."""
+        bounds FC2's persistent blocks (0: one an SM) to leave SMs to the collective.
+        transport: "nccl" (the two all-to-alls) or "peer": the pack kernel and FC2's epilogue store rows straight
+        into the receiving ranks' buffers over NVLink (CUDA IPC), flags mark each source done, and the waits
+        for them are bounded by wait_budget_ns (a late source is recorded in the error words, ops.err).  The
+        output is the same bytes.  "peer" needs max_tokens (tokens a rank, a call) for its fixed buffers."""
+        if transport not in ("nccl", "peer"):
+            raise ValueError(f"transport {transport!r}")
+        if transport == "peer" and (fixed_tokens is not None or overlap_chunks != 1 or not max_tokens):
+            raise ValueError("the peer transport takes the counts-exchange path, one FC2 pass, and max_tokens")
+        self.transport, self.max_tokens, self.wait_budget_ns = transport, max_tokens, int(wait_budget_ns)
+        self.peer = None
+        self.epoch = 0
         self.fixed_tokens = fixed_tokens
         self.group = group
         self.rank = dist.get_rank(group)
@@ -253,6 +377,15 @@ class EPMoELayer:
         self.ops = ops or GpuOps(device)
         self._side = None
         self.timing = None  # (dispatch_ms, combine_ms) of the last forward when events are given
+
+    def _forward_peer(self, S, x, events=None):
+        return _peer_forward(self, S, x, events)
+
+    def close(self):
+        """Unmap the peers' buffers (peer transport)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _route(self, idx):
         """(destination rank, local expert id at the destination) of every pick, int32 [T, K] each."""
@@ -324,6 +457,8 @@ class EPMoELayer:
         mode: "dispatch", "ffn", "combine")."""
         if self.fixed_tokens is not None:
             return self._forward_fixed(S, x, events)
+        if self.transport == "peer":
+            return self._forward_peer(S, x, events)
         ops, H, K, El, W = self.ops, self.H, self.K, self.E_local, self.world
         T = x.shape[0]
         idx, wts = ops.topk(S, self.bias, self.rs, K)
@@ -398,6 +533,76 @@ class EPMoELayer:
         ops.join(side, y, back)
         shared_rows = y[:, P_recv:P_all] if self.shared else None
         return ops.combine_chunked(back, send_pos, wts, shared_rows, T, K, H)
+
+
+def _peer_forward(layer, S, x, events=None):
+    """EPMoELayer.forward over peer memory (transport "peer"); see the class."""
+    ops, H, K, El, W, me = layer.ops, layer.H, layer.K, layer.E_local, layer.world, layer.rank
+    T = x.shape[0]
+    if T > layer.max_tokens:
+        raise ValueError(f"{T} tokens exceed max_tokens={layer.max_tokens}")
+    stride = ops.pair_stride(H, K)
+    if layer.peer is None:
+        layer.peer = PeerBuffers(W, me, W * layer.max_tokens + layer.max_tokens, stride, layer.max_tokens * K, H,
+                                 x.device, layer.group)
+        layer.shared_out = torch.empty((layer.max_tokens + 1, H), dtype=torch.bfloat16, device=x.device)
+    pb = layer.peer
+    layer.epoch = (layer.epoch + 1) & 0x7FFFFFFF
+    epoch = layer.epoch
+    idx, wts = ops.topk(S, layer.bias, layer.rs, K)
+    dest, lid = layer._route(idx)
+    plan = ops.tables(dest.reshape(-1, 1).contiguous(), W, 1)
+    send_pos = plan.exp2perm.reshape(T, K)
+    pairs = ops.pairs(dest.contiguous(), W)
+    rplan = ops.tables(pairs, W, 1)
+    counts = torch.stack([rplan.counts[:W], plan.counts[:W]], 1).to(torch.int32).contiguous()  # [W, 2]
+    every = torch.empty((W, W, 2), dtype=torch.int32, device=x.device)
+    dist.all_gather_into_tensor(every, counts, group=layer.group)
+    C = every.tolist()  # the one host synchronisation
+    lay = peer_offsets(C, me)
+    if max(lay["recv_rows"]) + layer.max_tokens > pb.cap_rows or max(lay["back_rows"]) > pb.back_cap:
+        raise ValueError("peer buffers too small for this step's routing")
+    R_recv, P_recv = lay["R_recv"], lay["P_recv"]
+    R_all, P_all = R_recv + (T if layer.shared else 0), P_recv + (T if layer.shared else 0)
+    row_base = [pb.recv_addr[d] + lay["shift"][d] * stride for d in range(W)]
+    if events:
+        events["dispatch"][0].record()
+    ops.pack_pairs_to(x, dest.contiguous(), lid.contiguous(), rplan.exp2perm.reshape(T, W), W, row_base, stride)
+    ops.signal(pb.flag_addr, W, me, 0, epoch)
+    ops.wait(pb.flags[:W], W, me, epoch, layer.wait_budget_ns)
+    if events:
+        events["dispatch"][1].record()
+    recv = pb.recv[:max(R_all, 1)]
+    if layer.shared:
+        ops.pack_pair_rows(x, K, El, recv[R_recv:R_all])
+    ids = ops.ids_k(recv, R_all, H, K)
+    tb = ops.tables(ids, El + layer.shared, 128)
+    qp, sfp = ops.unpack_k(recv, R_all, H, K, tb)
+    out_rows = ops.return_rows(tb, R_all, K)
+    layer.last = {"received_rows": R_recv, "received_picks": P_recv, "sent_rows": sum(c[0] for c in C[me]),
+                  "sent_picks": T * K, "tables": tb}
+    if events:
+        events["fc1"][0].record()
+    f1q, f1sf = ops.fc1_only(layer.w, qp, sfp, tb, H, layer.I, El + layer.shared)
+    if events:
+        events["fc1"][1].record()
+    row_bytes = H * 2
+    block_base = [pb.back_addr[s] + lay["back_row0"][s] * row_bytes for s in range(W)]
+    block_start = list(lay["pstart"])
+    if layer.shared:
+        block_base.append(layer.shared_out.data_ptr())
+        block_start.append(P_all)
+    sink = layer.shared_out[layer.max_tokens]
+    ptrs = ops.row_ptrs(tb, R_all, K, out_rows, block_base, block_start, row_bytes, sink)
+    ops.fc2_to_ptrs(layer.w, f1q, f1sf, tb, H, layer.I, El + layer.shared, ptrs)
+    if events:
+        events["combine"][0].record()
+    ops.signal(pb.flag_addr, W, me, W, epoch)
+    ops.wait(pb.flags[W:2 * W], W, me, epoch, layer.wait_budget_ns)
+    if events:
+        events["combine"][1].record()
+    shared_rows = layer.shared_out[:T] if layer.shared else None
+    return ops.combine(pb.back[:T * K], send_pos, wts, shared_rows, T, K, H)
 
 
 def slice_weights(w13, w13_sf, w2, w2_sf, E, shared, rank, world, H, I, owner=None):

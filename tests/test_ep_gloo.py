@@ -101,3 +101,64 @@ def test_ep2_gloo_matches_single_device(mode):
     c = cases.make_case(**_cfg(mode))
     ref, _ = cases.oracle_forward(c)
     assert np.array_equal(got, ref)
+
+
+def _late_worker(rank, world, port, outdir, mode):
+    """Rank 1 fails on the host before its step (mode "dead": exits; "silent": stays up but never posts its
+    sends); rank 0 runs the step and must come back with an error from the collective, within its timeout."""
+    import sys
+    import time
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    sys.path[:0] = [here, os.path.join(root, "oracle"), os.path.join(root, "kern-k3-pp-prefill_b200")]
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import cases as C
+    import ep_oracle_ops
+    import k3moe_ep
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    c = C.make_case(**CFG)
+    T_l = c.T // world
+    rows = slice(rank * T_l, (rank + 1) * T_l)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+    w = k3moe_ep.slice_weights(t(c.w13), t(c.w13_sf), t(c.w2), t(c.w2_sf), c.E, c.shared, rank, world, c.H, c.I)
+    rs = t(np.array([c.rs_bits], np.uint16)).view(torch.bfloat16)
+    layer = k3moe_ep.EPMoELayer(c.H, c.I, c.E, c.K, c.shared, w, t(c.bias), rs, ops=ep_oracle_ops.OracleOps())
+    if rank == 1:
+        if mode == "silent":
+            time.sleep(12)
+        os._exit(0)
+    t0 = time.time()
+    try:
+        layer.forward(t(c.S[rows]), t(c.x_bits[rows]).view(torch.bfloat16))
+        msg = "no error"
+    except Exception as ex:  # the collective's failure, seen on the host
+        msg = f"raised {type(ex).__name__}"
+    open(os.path.join(outdir, "rank0"), "w").write(f"{msg} after {time.time() - t0:.1f} s")
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["dead", "silent"])
+def test_ep_rank_that_never_sends_fails_on_the_host(mode):
+    """Failure detection on the host: a rank that exits, or never posts its sends, makes the other rank's step
+    end in an exception from the collective (process-group timeout 3 s), not a hang."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=_late_worker, args=(r, 2, port, d, mode)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(60)
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        got = open(os.path.join(d, "rank0")).read()
+        assert got.startswith("raised"), got
+        assert float(got.split(" after ")[1].split()[0]) < 30.0, got

@@ -45,3 +45,39 @@ def test_pair_plan_rows_per_token(world, K):
     for r in range(world):  # rank r's slots: one block, tokens in order
         s = plan["exp2perm"][:, r][pairs[:, r] >= 0]
         assert (np.diff(s) == 1).all()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8, 16])
+def test_peer_offsets_reproduce_the_all_to_all_layouts(world):
+    """The peer transport's store addresses (k3moe_ep.peer_offsets) put every dispatched row and every returned
+    result where the two all-to-alls would: received rows grouped by source rank, results grouped by the rank
+    that computed them, each block in its sender's order.  Checked against a simulation of the all-to-alls for
+    random count matrices, empty blocks included."""
+    rng = np.random.default_rng(world)
+    for trial in range(20):
+        C = rng.integers(0, 5, (world, world, 2))
+        C[:, :, 1] += C[:, :, 0]          # picks >= rows (a row carries one or more picks)
+        if trial % 4 == 0:
+            C[rng.integers(0, world), :, :] = 0   # a rank that sends nothing
+        lay = [k3moe_ep.peer_offsets(C.tolist(), r) for r in range(world)]
+        # dispatch: source s's slot p for rank d (slots grouped by destination) -> row p + shift[d] at d
+        for d in range(world):
+            want = [(s, j) for s in range(world) for j in range(C[s, d, 0])]   # the all-to-all's receive order
+            got = {}
+            for s in range(world):
+                slot0 = int(C[s, :d, 0].sum())
+                for j in range(C[s, d, 0]):
+                    got[slot0 + j + lay[s]["shift"][d]] = (s, j)
+            assert [got[i] for i in range(len(want))] == want and len(got) == len(want)
+            assert lay[d]["R_recv"] == len(want) == lay[0]["recv_rows"][d]
+        # combine: at computing rank d, result q of source s (q in [pstart[s], pstart[s+1])) -> row
+        # back_row0[s] + q - pstart[s] of s's return buffer, which the all-to-all fills grouped by computing rank
+        for s in range(world):
+            want = [(d, j) for d in range(world) for j in range(C[s, d, 1])]
+            got = {}
+            for d in range(world):
+                L = lay[d]
+                for q in range(L["pstart"][s], L["pstart"][s + 1]):
+                    got[L["back_row0"][s] + q - L["pstart"][s]] = (d, q - L["pstart"][s])
+            assert [got[i] for i in range(len(want))] == want and len(got) == len(want)
+            assert lay[0]["back_rows"][s] == len(want)

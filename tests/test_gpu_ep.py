@@ -1,9 +1,11 @@
 """Expert parallelism on 2 GPUs over NCCL: every rank holds half the experts
 and its own tokens; the layer's output must equal, bit for bit, the single-GPU
-layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs.  Four
-modes: the counts-exchange all-to-all, the fixed-block all-to-all, the
-fixed-block step captured in a CUDA graph (NCCL calls inside) and replayed,
-and experts dealt to the ranks by router bias instead of contiguous blocks."""
+layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs.  Modes: the
+counts-exchange all-to-all, the fixed-block all-to-all, the fixed-block step
+captured in a CUDA graph (NCCL calls inside) and replayed, experts dealt to
+the ranks by router bias instead of contiguous blocks, FC2 in column slices
+returned beside the next slice, and the peer-memory transport (rows and
+results stored into the peers' buffers over NVLink, flags, bounded waits)."""
 import multiprocessing as mp
 import os
 import socket
@@ -63,7 +65,9 @@ def _worker(rank, world, port, outdir, mode):
     layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev,
                                 fixed_tokens=c["T_local"] if mode in ("fixed", "graph") else None, owner=owner,
                                 overlap_chunks=2 if mode == "overlap" else 1,
-                                fc2_grid_cap=100 if mode == "overlap" else 0)
+                                fc2_grid_cap=100 if mode == "overlap" else 0,
+                                transport="peer" if mode == "peer" else "nccl",
+                                max_tokens=c["T_local"] if mode == "peer" else None)
     xs, Ss = x[rows].contiguous(), S[rows].contiguous()
     graph = None
     if mode == "graph":
@@ -97,6 +101,12 @@ def _worker(rank, world, port, outdir, mode):
         ok = ok and not bad_rows
         open(os.path.join(outdir, "result"), "w").write(
             "ok" if ok else f"mismatch: repeat-equal={ok} rows={bad_rows[:20]} n={len(bad_rows)} maxdiff={diff}")
+    if mode == "peer":  # the waits recorded nothing, and the peers' buffers are unmapped before the group goes
+        words = layer.ops.err[:2].tolist()
+        if rank == 0 and words != [0, 0]:
+            open(os.path.join(outdir, "result"), "w").write(f"device error words {words}")
+        dist.barrier()
+        layer.close()
     if graph is not None:  # a graph holding NCCL calls is released before the process group goes
         graph.reset()
     del graph
@@ -105,7 +115,7 @@ def _worker(rank, world, port, outdir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed", "overlap"])
+@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed", "overlap", "peer"])
 def test_ep2_nccl_bit_identical_to_one_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

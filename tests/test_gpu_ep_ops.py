@@ -134,3 +134,102 @@ def test_pair_rows_plan_pack_unpack_return(setup):
     ret_o = _np(oops.return_rows(tb_o, R, K))
     assert np.array_equal(ret_g[rows], ret_o[rows])
     assert np.array_equal(np.sort(ret_g[rows]), np.arange(rows.size))
+
+
+# ------------------------------------------------------------------ the peer-memory transport's kernels, one GPU
+def test_pack_pairs_to_lands_rows_where_the_all_to_all_would(setup):
+    """k3moe_ep_pack_pairs_to with every rank's receive buffer local (three ranks' buffers on this GPU, this
+    rank = 1): the rows for rank d land at peer_offsets' shift, the same bytes as the contiguous pack."""
+    c, g, gops, oops = setup
+    Wn, me = 3, 1
+    idx, wts = gops.topk(g["S"], g["bias"], g["rs"], K)
+    dest = (idx % Wn).to(torch.int32).contiguous()
+    lid = (idx // Wn).to(torch.int32).contiguous()
+    pairs = gops.pairs(dest, Wn)
+    rplan = gops.tables(pairs, Wn, 1)
+    rows_to = rplan.counts[:Wn].tolist()
+    n = sum(rows_to)
+    flat = gops.pack_pairs(g["x"], dest, lid, rplan.exp2perm.reshape(c.T, Wn), Wn, n)
+    st = flat.shape[1]
+    # counts of the other two (made-up) ranks, so this rank's rows land after theirs at some destinations
+    C = [[(5, 9), (0, 0), (3, 4)], [(r, r) for r in rows_to], [(2, 2), (7, 8), (0, 0)]]
+    lay = k3moe_ep.peer_offsets(C, me)
+    bufs = [torch.full((lay["recv_rows"][d] + 4, st), 0xA5, dtype=torch.uint8, device=flat.device) for d in range(Wn)]
+    base = [bufs[d].data_ptr() + lay["shift"][d] * st for d in range(Wn)]
+    gops.pack_pairs_to(g["x"], dest, lid, rplan.exp2perm.reshape(c.T, Wn), Wn, base, st)
+    torch.cuda.synchronize()
+    used = H + H // 32 + 2 * K
+    slot0 = 0
+    for d in range(Wn):
+        land = sum(C[s][d][0] for s in range(me))
+        got = bufs[d][land:land + rows_to[d], :used]
+        assert torch.equal(got, flat[slot0:slot0 + rows_to[d], :used]), f"destination {d}"
+        assert bool((bufs[d][:land] == 0xA5).all()) and bool((bufs[d][land + rows_to[d]:] == 0xA5).all())
+        slot0 += rows_to[d]
+
+
+def test_fc2_to_row_pointers_equals_fc2_to_rows(setup):
+    """FC2 storing each permuted row through a pointer table (k3moe_ep_row_ptrs over three blocks + the shared
+    block) equals FC2 storing row out_rows[r] of one buffer."""
+    c, g, gops, oops = setup
+    idx, _ = gops.topk(g["S"], g["bias"], g["rs"], K)
+    tb = k3moe.route_tables(idx, E, 0, SH)
+    qp, sfp = k3moe.quant_permute(g["x"], tb)
+    f1q, f1sf = k3moe.fc1(g["w13"], g["w13_sf"], qp, sfp, tb, H, I, E + SH, gops.err)
+    out_rows = gops.return_rows(tb, c.T, K)
+    P = c.T * K
+    P_all = P + c.T
+    ref = torch.zeros((P_all, H), dtype=torch.bfloat16, device=qp.device)
+    k3moe._check(k3moe.lib().k3moe_fc2_to_rows(
+        g["w2"].data_ptr(), g["w2_sf"].data_ptr(), f1q.data_ptr(), f1sf.data_ptr(), tb.cta_batch.data_ptr(),
+        tb.cta_limit.data_ptr(), tb.meta.data_ptr(), out_rows.data_ptr(), ref.data_ptr(), H, I, E + SH, tb.cap_rows,
+        tb.max_ctas, gops.err.data_ptr(), k3moe._stream()), "fc2_to_rows")
+    # the same rows split over four buffers: results [0, a), [a, b), [b, P) and the shared rows [P, P_all)
+    cuts = [0, P // 3, (2 * P) // 3, P, P_all]
+    bufs = [torch.zeros((cuts[i + 1] - cuts[i] + 3, H), dtype=torch.bfloat16, device=qp.device) for i in range(4)]
+    sink = torch.zeros(H, dtype=torch.bfloat16, device=qp.device)
+    ptrs = gops.row_ptrs(tb, c.T, K, out_rows, [b.data_ptr() + 3 * H * 2 for b in bufs], cuts, H * 2, sink)
+    gops.fc2_to_ptrs(g, f1q, f1sf, tb, H, I, E + SH, ptrs)
+    torch.cuda.synchronize()
+    assert gops.err[:2].tolist() == [0, 0]
+    for i in range(4):
+        assert torch.equal(bufs[i][3:].view(torch.int16), ref[cuts[i]:cuts[i + 1]].view(torch.int16)), f"block {i}"
+        assert bool((bufs[i][:3] == 0).all())
+    assert bool((sink == 0).all())
+
+
+def test_signal_writes_the_peers_slots(dev):
+    Wn, me, epoch = 4, 2, 7
+    flags = [torch.zeros(2 * Wn, dtype=torch.int32, device=dev) for _ in range(Wn)]
+    ops = k3moe_ep.GpuOps(dev)
+    ops.signal([f.data_ptr() for f in flags], Wn, me, Wn, epoch)
+    torch.cuda.synchronize()
+    for s in range(Wn):
+        want = [0] * (2 * Wn)
+        if s != me:
+            want[Wn + me] = epoch
+        assert flags[s].tolist() == want
+
+
+def test_wait_returns_an_error_when_a_flag_is_never_set(dev):
+    """Failure detection on the device: a wait whose flags nothing sets gives up after its 1 ms budget, records
+    the late source in the error words and returns; the context stays usable and the host reads the status."""
+    import time
+
+    Wn, skip = 4, 0
+    flags = torch.zeros(Wn, dtype=torch.int32, device=dev)
+    flags[1] = 3  # source 1 arrived; 2 and 3 never do
+    ops = k3moe_ep.GpuOps(dev)
+    t0 = time.perf_counter()
+    ops.wait(flags, Wn, skip, 3, 1_000_000)
+    rc, words = k3moe.read_error(ops.err)
+    dt = time.perf_counter() - t0
+    assert rc == -6 and words[0] & 1 and words[1] in (0xA02, 0xA03), (rc, [hex(w) for w in words])
+    assert dt < 2.0
+    # the context still works, and a wait whose flags are all set records nothing
+    flags.fill_(3)
+    ops.wait(flags, Wn, skip, 3, 1_000_000)
+    rc, words = k3moe.read_error(ops.err)
+    assert rc == 0 and words == (0, 0)
+    x = torch.ones(1024, device=dev)
+    assert float(x.sum().item()) == 1024.0
