@@ -66,6 +66,15 @@ int k3moe_abi_version(void);
 int k3moe_route_topk(const float* S, int lds, const float* bias, const void* rs_bf16, int T, int E_total, int K,
                      int32_t* idx, float* wts, k3moe_stream_t stream);
 
+/* ---------------------------------------------------------------- the router GEMM
+ * S[t, e] = sum_h x[t, h] * W[e, h]: bf16 x bf16 -> f32 on the tensor cores (x [T, ldx], W [E, ldw], S
+ * [T, lds]), the logits the top-k reads.  H a multiple of 64, E of 16; ldx, ldw multiples of 8 and lds of 4;
+ * pointers 16-byte aligned.  err: the device error words (a bounded wait that ran out), or null.
+ * Replaces: the router projection gemm(L + "router", normed, w_router, router_partial, EXPERTS, H)
+ *   (scripts/gen_stage.py:1130), bound to extern:cublas_bf16_tn_f32 (gen_stage.py:244-247). */
+int k3moe_router_gemm(const void* x_bf16, int ldx, const void* w_bf16, int ldw, int T, int E, int H, float* S, int lds,
+                      uint32_t* err, k3moe_stream_t stream);
+
 /* ---------------------------------------------------------------- routing tables
  * Over R rows with K ids each (global expert indices), the local experts being
  * [first, first + E): counts[e], the CTA tables of `tile`-row tiles,
@@ -149,16 +158,17 @@ int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_pe
                   uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
                   int activation, k3moe_stream_t stream);
 
-/* The two TMA descriptors (128 bytes each: the weights', then the activations') that the module entries
- * kern_k3_moe_fc1 / kern_k3_moe_fc2 of k3moe_module.cubin read through their `maps` argument, encoded for
- * buffers at fixed addresses and copied to maps_dev (256 bytes of device memory, 64-byte aligned): a load-time
- * call, once the buffers are placed; it synchronises `stream`.  mode 0: FC1 over w = W13 [n_experts*2I, H/2]
+/* The nine TMA descriptors (128 bytes each: the weights', then the activations' with boxes of 16, 32, ...,
+ * 128 rows) that the module entries kern_k3_moe_fc1 / kern_k3_moe_fc2 of k3moe_module.cubin read through their
+ * `maps` argument, encoded for buffers at fixed addresses and copied to maps_dev (K3MOE_GEMM_MAPS_BYTES of
+ * device memory, 64-byte aligned): a load-time call, once the buffers are placed; it synchronises `stream`.  mode 0: FC1 over w = W13 [n_experts*2I, H/2]
  * and act = q_perm [cap_rows, H]; mode 1: FC2 over w = W2 [n_experts*H, I/2] and act = fc1_q [cap_rows, I].
  * The module entries take the reference ops' parameter lists (scripts/k3_moe_bmm.py:131-134, 167-169) and
  * replace the trtllm_bmm launches of scripts/k3_moe_bmm.py:112-113, whose 17,472-byte parameter block carries
  * its own descriptors (docs/k3-kernel-abi.md:549-565). */
 #define K3MOE_GEMM_THREADS 384        /* block of kern_k3_moe_fc1 / kern_k3_moe_fc2 */
 #define K3MOE_GEMM_SMEM_BYTES 204032  /* their dynamic shared memory */
+#define K3MOE_GEMM_MAPS_BYTES 1152    /* their descriptor buffer */
 int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n_experts, int H, int I, int cap_rows,
                            void* maps_dev, k3moe_stream_t stream);
 

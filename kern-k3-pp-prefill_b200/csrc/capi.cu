@@ -11,6 +11,7 @@
 #include "route.cu"
 #include "ep.cu"
 #include "ep_peer.cu"
+#include "router.cu"
 #include "dropin.cu"
 
 using namespace k3;
@@ -72,12 +73,13 @@ EncodeTiledFn encode_fn() {
 // Map over a tile-major operand (rows x k, both multiples of 128): viewed as
 // rows*k/128 rows of 128 elements, so one 128 x 128 box is one stored tile
 // (a contiguous 16 KB of E4M3 or 8 KB of packed E2M1); 128-byte swizzle.
-int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool fp4) {
+// box_rows < 128: the box covers the first box_rows rows of a tile.
+int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool fp4, int box_rows = 128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return K3MOE_EDRIVER;
   const cuuint64_t dims[2] = {128, (cuuint64_t)(rows * (k / 128))};
   const cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? 64 : 128)};
-  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -140,11 +142,14 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   if (out0 == nullptr || reinterpret_cast<uintptr_t>(out0) % 32 != 0) return K3MOE_EINVAL;
   const int K = mode == MODE_FC1 ? H : I;
   const int rows_per_expert = mode == MODE_FC1 ? 2 * I : H;
-  CUtensorMap ta, tb;
+  CUtensorMap ta;
+  ActMaps tb;
   int rc = encode_operand(&ta, w, (long long)n_experts * rows_per_expert, K, true);
   if (rc) return rc;
-  rc = encode_operand(&tb, act, cap_rows, K, false);
-  if (rc) return rc;
+  for (int m = 0; m < gemm::A_MAPS; ++m) {
+    rc = encode_operand(&tb.m[m], act, cap_rows, K, false, 16 * (m + 1));
+    if (rc) return rc;
+  }
   GemmParams p;
   p.sfw = w_sf;
   p.sfa = act_sf;
@@ -353,6 +358,57 @@ int k3moe_synth_mxfp4(uint64_t seed, long long row0, long long rows, int K, floa
   return launch_status();
 }
 
+int k3moe_router_gemm(const void* x_bf16, int ldx, const void* w_bf16, int ldw, int T, int E, int H, float* S, int lds,
+                      uint32_t* err, k3moe_stream_t stream) {
+  if (!x_bf16 || !w_bf16 || !S || T < 1 || E < 16 || E % 16 || H < 64 || H % 64 || ldx < H || ldx % 8 ||
+      ldw < H || ldw % 8 || lds < E || lds % 4 || reinterpret_cast<uintptr_t>(x_bf16) % 16 ||
+      reinterpret_cast<uintptr_t>(w_bf16) % 16 || reinterpret_cast<uintptr_t>(S) % 16)
+    return K3MOE_EINVAL;
+  // expert columns a unit: the largest multiple of 16 up to 256 dividing E (224 for 896)
+  int bn = 16;
+  for (int c = rgemm::BN_MAX; c >= 16; c -= 16)
+    if (E % c == 0) {
+      bn = c;
+      break;
+    }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return K3MOE_EDRIVER;
+  CUtensorMap mx, mw;
+  const cuuint32_t estr[2] = {1, 1};
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)T};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {rgemm::BK, rgemm::BM};
+    if (fn(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x_bf16), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return K3MOE_ETMAP;
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)H, (cuuint64_t)E};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldw * 2};
+    const cuuint32_t box[2] = {rgemm::BK, (cuuint32_t)bn};
+    if (fn(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w_bf16), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return K3MOE_ETMAP;
+  }
+  RouterParams p;
+  p.S = S;
+  p.lds = lds;
+  p.T = T;
+  p.K = H;
+  p.bn = bn;
+  p.n_tiles = E / bn;
+  p.m_tiles = (int)cdiv(T, rgemm::BM);
+  p.err = err;
+  const int units = p.m_tiles * p.n_tiles;
+  const int grid = std::min(units, num_sms(current_device()));
+  if (!set_smem_once(router_gemm_kernel, rgemm::SMEM_BYTES, 3)) return K3MOE_ELAUNCH;
+  router_gemm_kernel<<<grid, rgemm::THREADS, rgemm::SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(mx, mw, p);
+  return launch_status();
+}
+
 int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n_experts, int H, int I, int cap_rows,
                            void* maps_dev, k3moe_stream_t stream) {
   if ((mode != 0 && mode != 1) || !w || !act || !maps_dev || n_experts < 1 || H < 256 || H % 256 || I < 256 ||
@@ -360,11 +416,14 @@ int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n
     return K3MOE_EINVAL;
   const int K = mode == 0 ? H : I;
   const int rows_per_expert = mode == 0 ? 2 * I : H;
-  CUtensorMap maps[2];
+  CUtensorMap maps[1 + gemm::A_MAPS];
+  static_assert(sizeof(maps) == K3MOE_GEMM_MAPS_BYTES, "the descriptor buffer's size in include/k3moe.h");
   int rc = encode_operand(&maps[0], w, (long long)n_experts * rows_per_expert, K, true);
   if (rc) return rc;
-  rc = encode_operand(&maps[1], act, cap_rows, K, false);
-  if (rc) return rc;
+  for (int m = 0; m < gemm::A_MAPS; ++m) {
+    rc = encode_operand(&maps[1 + m], act, cap_rows, K, false, 16 * (m + 1));
+    if (rc) return rc;
+  }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemcpyAsync(maps_dev, maps, sizeof(maps), cudaMemcpyHostToDevice, s) != cudaSuccess) return K3MOE_ELAUNCH;
   return cudaStreamSynchronize(s) == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH;

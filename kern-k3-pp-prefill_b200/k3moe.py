@@ -76,6 +76,7 @@ SIGNATURES = {
     "k3moe_ipc_export": (_I, [_P, _P, _P]),
     "k3moe_ipc_import": (_I, [_P, _U64, _P]),
     "k3moe_ipc_release": (_I, [_P, _U64]),
+    "k3moe_router_gemm": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _P]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",
@@ -149,6 +150,16 @@ def route_topk(S: torch.Tensor, bias: torch.Tensor, rs: torch.Tensor, K: int, E:
     _check(lib().k3moe_route_topk(_p(S), S.stride(0), _p(bias), _p(rs), T, E, K, _p(idx), _p(wts), _stream(stream)),
            "route_topk")
     return idx, wts
+
+
+def router_gemm(x: torch.Tensor, w: torch.Tensor, err: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """S = x . w^T in f32 (x bf16 [T, H], w bf16 [E, H]): the router logits (k3moe_router_gemm)."""
+    T, H = x.shape
+    E = w.shape[0]
+    S = torch.empty((T, E), dtype=torch.float32, device=x.device)
+    _check(lib().k3moe_router_gemm(_p(x), x.stride(0), _p(w), w.stride(0), T, E, H, _p(S), S.stride(0), _p(err),
+                                   _stream(stream)), "router_gemm")
+    return S
 
 
 @dataclass

@@ -68,10 +68,11 @@ def reference_weights(packed: torch.Tensor, sf: torch.Tensor, experts: int, n: i
 
 
 def pack_topk(idx: torch.Tensor, wts: torch.Tensor) -> torch.Tensor:
-    """Top-k ids and weights packed as FlashInfer's routed entry reads them: bf16 weight bits in the high
-    16 bits, the expert id in the low 16."""
+    """Top-k ids and weights packed as FlashInfer's routed entry reads them: the expert id in the high 16
+    bits, the weight's bf16 bits in the low 16 (the packing FlashInfer's own tuner makes,
+    fused_moe/core.py `_init_packed_topk_ids`)."""
     wb = wts.to(torch.bfloat16).view(torch.int16).to(torch.int32) & 0xFFFF
-    return ((wb << 16) | (idx.to(torch.int32) & 0xFFFF)).contiguous()
+    return ((idx.to(torch.int32) << 16) | wb).contiguous()
 
 
 class ReferenceMoE:
@@ -89,7 +90,7 @@ class ReferenceMoE:
         """q_fp8 [T, H] float8_e4m3fn, sf_linear [T, H/32] (UE8M0 bytes), topk_packed [T, K] int32.
         finalize: the combined bf16 output [T, H]; else (FC2 rows [padded, H], expanded->permuted row map)."""
         out = self.fm.trtllm_fp4_block_scale_routed_moe(
-            topk_packed, None, q_fp8, sf_linear, self.g1, self.g1s, None, None, None, None, self.g2, self.g2s,
+            topk_packed, None, q_fp8, sf_linear.view(torch.float8_e4m3fn), self.g1, self.g1s, None, None, None, None, self.g2, self.g2s,
             None, None, None, None, self.E, self.K, None, None, self.I, 0, self.E, None,
             routing_method_type=1, do_finalize=finalize, tune_max_num_tokens=tune_max)
         return out[0] if finalize else (out[0], out[2])

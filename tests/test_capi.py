@@ -83,3 +83,19 @@ def test_ep_and_gemm_argument_checks(lib):
     assert lib.k3moe_fc2(None, None, None, None, None, None, None, 16, 7168, 2048, 8, 1024, 8, None, None) == -1
     assert lib.k3moe_combine_ep_chunked(None, 0, 100, None, None, None, 0, 0, None, 7168, 4, 8, 7168, 1000,
                                         None) == -1
+
+
+def test_noalloc_limits_match_the_header():
+    """The Python mirror's limits of the allocation-free entry are the header's, and the fixed array (513 KB,
+    2 x 256-byte-rounded [R/256][E + shared] int tables) is exactly the scratch of the largest call."""
+    import os
+    import re
+
+    import k3moe
+
+    hdr = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "k3moe.h")).read()
+    rows = int(re.search(r"#define K3MOE_NOALLOC_MAX_ROWS (\d+)", hdr).group(1))
+    experts = int(re.search(r"#define K3MOE_NOALLOC_MAX_EXPERTS (\d+)", hdr).group(1))
+    assert (rows, experts) == (k3moe.NOALLOC_MAX_ROWS, k3moe.NOALLOC_MAX_EXPERTS)
+    assert k3moe.lib().k3moe_route_scratch_bytes(rows, experts - 1, 1) == 2 * -(-(rows // 256) * experts * 4 // 256) * 256
+    assert k3moe.lib().k3moe_route_scratch_bytes(rows, experts - 1, 1) == 524800

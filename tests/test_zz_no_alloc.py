@@ -60,3 +60,14 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(dev):
     rc = lib.k3moe_route_tables_noalloc(ids.data_ptr(), 128, 1, 0, k3moe.NOALLOC_MAX_EXPERTS, 1, 128, p, p, p, p,
                                         p, p, s)
     assert rc == -7
+
+
+def test_noalloc_at_its_limits(dev):
+    """The largest call the fixed array takes (K3MOE_NOALLOC_MAX_ROWS rows, K3MOE_NOALLOC_MAX_EXPERTS local
+    experts with the shared expert): its second scratch table ends exactly at the end of the array."""
+    R, E = k3moe.NOALLOC_MAX_ROWS, k3moe.NOALLOC_MAX_EXPERTS - 1
+    ids = torch.from_numpy(_ids(R, 8, E, 3)).to(dev)
+    got = k3moe.route_tables_noalloc(ids, E, 0, 1)
+    ref = k3moe.route_tables(ids, E, 0, 1)
+    torch.cuda.synchronize()
+    _same(got, ref)
