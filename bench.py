@@ -152,7 +152,8 @@ def host_inputs(T, E, seed_x, seed_router=7):
     bias = rr.uniform(-0.1, 0.1, E).astype(np.float32)
     xf = (x_bits.astype(np.uint32) << 16).view(np.float32)
     S = np.ascontiguousarray(xf @ wr, dtype=np.float32)
-    return {"x_bits": x_bits, "S": S, "bias": bias, "rs_bits": int(bf16_round(np.array([RS], np.float32))[0])}
+    return {"x_bits": x_bits, "S": S, "bias": bias, "rs_bits": int(bf16_round(np.array([RS], np.float32))[0]),
+            "w_router": wr}
 
 
 def device_inputs(h, dev):
@@ -905,6 +906,46 @@ def run_native(args, dev):
     print(json.dumps(line), flush=True)
 
 
+def router_gemm_timing(x, wr, dev, n=20):
+    """The router GEMM S = x . W_router^T (bf16 in, f32 out, k3moe_router_gemm) timed with CUDA events, against
+    cuBLAS's bf16 GEMM of the same operands (torch.mm, bf16 out), and checked against an f32 matmul."""
+    import torch
+
+    import k3moe
+
+    w = torch.from_numpy(bf16_round(np.ascontiguousarray(wr.T)).view(np.int16)).to(dev).view(torch.bfloat16)
+    T, Hh = x.shape
+    E_ = w.shape[0]
+    err = torch.zeros(4, dtype=torch.int32, device=dev)
+    S = k3moe.router_gemm(x, w, err)
+    ref = x.float() @ w.float().t()
+    rel = float((S - ref).norm() / ref.norm())
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    ms = timed(lambda: k3moe.router_gemm(x, w, err))
+    ms_cublas = timed(lambda: torch.mm(x, w.t()))
+    flop = 2.0 * T * Hh * E_
+    try:
+        peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+        kind = "measured"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    return {"ms": ms, "tflops": flop / ms / 1e9, "cublas_bf16_out_ms": ms_cublas, "vs_cublas": ms_cublas / ms,
+            "frac_of_bf16_peak": flop / ms / 1e9 / peak, "peak_kind": kind, "rel_l2_vs_f32": rel,
+            "device_error_words": err[:2].tolist(), "shape": [T, Hh, E_]}
+
+
 TRAFFIC_SOURCE = ("ncu DRAM bytes (read + write) per algorithmic byte of FC1 on the small-case capture "
                   "(profiles/grouped_gemm_fc1_fc2_small_case.md), times this launch's algorithmic bytes")
 
@@ -1067,6 +1108,10 @@ def main():
     e2e_ms = e2e_overlapped(fwd, S_h, x_h, (T, H), e2e_steps, stream, dev)
     layer.check_device_error(T)
 
+    # ---------------- the router GEMM (the step before the path, outside the layer's time): this build's
+    # tcgen05 kernel against cuBLAS (torch.mm, bf16 out) on the same x and W_router (bf16)
+    router = router_gemm_timing(x, hin["w_router"], dev)
+
     # ---------------- the CPU leg (after timing): the oracle checks this run's own intermediates on sampled
     # token tiles and every row's routing, and its FC1 + FC2 time over the sample is the CPU baseline
     cpu, parity = None, None
@@ -1106,6 +1151,7 @@ def main():
                 "copies": "every step's x, S in and output back over PCIe, on side streams overlapping the "
                           "neighbouring steps' compute (double buffers)"},
         "gpu_launches": 8 * args.steps,
+        "router_gemm": router,
         "gemm_trace": gemm_trace,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,

@@ -158,9 +158,8 @@ int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_pe
                   uint8_t* fc1_sf, int H, int I, int n_experts, int cap_rows, int max_ctas, uint32_t* err,
                   int activation, k3moe_stream_t stream);
 
-/* The nine TMA descriptors (128 bytes each: the weights', then the activations' with boxes of 16, 32, ...,
- * 128 rows) that the module entries kern_k3_moe_fc1 / kern_k3_moe_fc2 of k3moe_module.cubin read through their
- * `maps` argument, encoded for buffers at fixed addresses and copied to maps_dev (K3MOE_GEMM_MAPS_BYTES of
+/* The two TMA descriptors (128 bytes each: the weights', then the activations') that the module entries
+ * kern_k3_moe_fc1 / kern_k3_moe_fc2 of k3moe_module.cubin read through their `maps` argument, encoded for buffers at fixed addresses and copied to maps_dev (K3MOE_GEMM_MAPS_BYTES of
  * device memory, 64-byte aligned): a load-time call, once the buffers are placed; it synchronises `stream`.  mode 0: FC1 over w = W13 [n_experts*2I, H/2]
  * and act = q_perm [cap_rows, H]; mode 1: FC2 over w = W2 [n_experts*H, I/2] and act = fc1_q [cap_rows, I].
  * The module entries take the reference ops' parameter lists (scripts/k3_moe_bmm.py:131-134, 167-169) and
@@ -168,7 +167,7 @@ int k3moe_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_pe
  * its own descriptors (docs/k3-kernel-abi.md:549-565). */
 #define K3MOE_GEMM_THREADS 384        /* block of kern_k3_moe_fc1 / kern_k3_moe_fc2 */
 #define K3MOE_GEMM_SMEM_BYTES 204032  /* their dynamic shared memory */
-#define K3MOE_GEMM_MAPS_BYTES 1152    /* their descriptor buffer */
+#define K3MOE_GEMM_MAPS_BYTES 256     /* their descriptor buffer */
 int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n_experts, int H, int I, int cap_rows,
                            void* maps_dev, k3moe_stream_t stream);
 

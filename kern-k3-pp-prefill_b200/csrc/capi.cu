@@ -73,13 +73,12 @@ EncodeTiledFn encode_fn() {
 // Map over a tile-major operand (rows x k, both multiples of 128): viewed as
 // rows*k/128 rows of 128 elements, so one 128 x 128 box is one stored tile
 // (a contiguous 16 KB of E4M3 or 8 KB of packed E2M1); 128-byte swizzle.
-// box_rows < 128: the box covers the first box_rows rows of a tile.
-int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool fp4, int box_rows = 128) {
+int encode_operand(CUtensorMap* m, const void* base, long long rows, int k, bool fp4) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return K3MOE_EDRIVER;
   const cuuint64_t dims[2] = {128, (cuuint64_t)(rows * (k / 128))};
   const cuuint64_t strides[1] = {(cuuint64_t)(fp4 ? 64 : 128)};
-  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  const cuuint32_t box[2] = {128, 128};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -142,14 +141,11 @@ int gemm_launch(int mode, const uint8_t* w, const uint8_t* w_sf, const uint8_t* 
   if (out0 == nullptr || reinterpret_cast<uintptr_t>(out0) % 32 != 0) return K3MOE_EINVAL;
   const int K = mode == MODE_FC1 ? H : I;
   const int rows_per_expert = mode == MODE_FC1 ? 2 * I : H;
-  CUtensorMap ta;
-  ActMaps tb;
+  CUtensorMap ta, tb;
   int rc = encode_operand(&ta, w, (long long)n_experts * rows_per_expert, K, true);
   if (rc) return rc;
-  for (int m = 0; m < gemm::A_MAPS; ++m) {
-    rc = encode_operand(&tb.m[m], act, cap_rows, K, false, 16 * (m + 1));
-    if (rc) return rc;
-  }
+  rc = encode_operand(&tb, act, cap_rows, K, false);
+  if (rc) return rc;
   GemmParams p;
   p.sfw = w_sf;
   p.sfa = act_sf;
@@ -416,14 +412,12 @@ int k3moe_gemm_tensor_maps(int mode, const uint8_t* w, const uint8_t* act, int n
     return K3MOE_EINVAL;
   const int K = mode == 0 ? H : I;
   const int rows_per_expert = mode == 0 ? 2 * I : H;
-  CUtensorMap maps[1 + gemm::A_MAPS];
+  CUtensorMap maps[2];
   static_assert(sizeof(maps) == K3MOE_GEMM_MAPS_BYTES, "the descriptor buffer's size in include/k3moe.h");
   int rc = encode_operand(&maps[0], w, (long long)n_experts * rows_per_expert, K, true);
   if (rc) return rc;
-  for (int m = 0; m < gemm::A_MAPS; ++m) {
-    rc = encode_operand(&maps[1 + m], act, cap_rows, K, false, 16 * (m + 1));
-    if (rc) return rc;
-  }
+  rc = encode_operand(&maps[1], act, cap_rows, K, false);
+  if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemcpyAsync(maps_dev, maps, sizeof(maps), cudaMemcpyHostToDevice, s) != cudaSuccess) return K3MOE_ELAUNCH;
   return cudaStreamSynchronize(s) == cudaSuccess ? K3MOE_OK : K3MOE_ELAUNCH;

@@ -54,15 +54,7 @@ constexpr int SF_STAGE = 3 * SF_BYTES;                        // activation atom
 // TMA unit three large boxes a stage (measured 1.5% faster a layer than six TMA operations); 0: all by TMA.
 // Moving the 16 KB activation tile to cp.async as well starved the MMA (FC1 3.06 -> 3.94 ms).
 constexpr int LDGSTS = K3MOE_LDGSTS;
-// A tile's activation rows are loaded in one box of roundup(rows, 16) rows: A_MAPS tensor maps with boxes of
-// 16, 32, ..., 128 rows, so a partly filled tile (at config 1 most experts hold ~73 rows) writes only its rows
-// into shared memory, whose port the TMA fill and the tensor core's operand reads share.  The rows past the
-// box keep a previous stage's bytes: their accumulator rows are computed and never stored.
-constexpr int A_MAPS = BM / 16;
-// bytes a stage's copies complete on its barrier with an activation box of `rows` rows
-__host__ __device__ constexpr u32 stage_tx(int rows) {
-  return (u32)(rows * BK + B_BYTES / 2 + (LDGSTS ? 0 : SF_STAGE));
-}
+constexpr u32 STAGE_TX = LDGSTS ? A_BYTES + B_BYTES / 2 : A_BYTES + B_BYTES / 2 + SF_STAGE;
 constexpr int SMEM_BYTES = STAGES * (OPS_STAGE + SF_STAGE) + 1024 /*align*/ + 256 /*barriers*/;
 constexpr u32 TMEM_COLS = 512;
 constexpr int SF_TMEM_COL = BN;          // scale columns after the accumulator
@@ -134,9 +126,8 @@ __device__ __forceinline__ int weight_row(const GemmParams& p, const Unit& w, in
   return w.e * p.rows_per_expert + (p.fb0 + w.fb) * gemm::BN + h * 128;
 }
 
-// The kernel body: tmW points at the weight tensor map, tmA at the A_MAPS activation maps (box heights 16, 32,
-// ..., 128 rows): kernel parameters for the C-ABI launch, a global-memory descriptor buffer for the module
-// entries of module_gemm.cu.
+// The kernel body: tmW / tmA point at the weight and activation tensor maps (kernel parameters for the C-ABI
+// launch, a global-memory descriptor buffer for the module entries of module_gemm.cu).
 template <int MODE>
 __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmA, const GemmParams& p) {
   using namespace gemm;
@@ -169,7 +160,7 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(tmW);
-    for (int m = 0; m < A_MAPS; ++m) prefetch_tmap(tmA + m);
+    prefetch_tmap(tmA);
   }
   tc_fence_before();
   __syncthreads();
@@ -197,19 +188,18 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
         int wrow[2];
         wrow[0] = weight_row<MODE>(p, w, 0);
         wrow[1] = weight_row<MODE>(p, w, 1);
-        const int abox = (w.n + 15) >> 4;  // the activation box: abox * 16 rows (w.n in 1..128)
         for (int ks = 0; ks < kstages; ++ks) {
           const long long t0 = clock64();
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, 0x200u + MODE)) break;
           t_wait += clock64() - t0;
           uint8_t* st = ops + stage * OPS_STAGE;
           uint8_t* sf = sfs + stage * SF_STAGE;
-          mbar_arrive_expect_tx(&full[stage], stage_tx(abox * 16));
+          mbar_arrive_expect_tx(&full[stage], STAGE_TX);
           ++armed[stage];
           // tile-major operands: tile t = row_block * kstages + ks is rows [128 t, 128 t + 128) of the
           // maps (one contiguous chunk), and its scales are the 512-byte atom t
           const int ta = (w.row0 / BM) * kstages + ks;
-          tma_load_2d(st, tmA + (abox - 1), &full[stage], 0, ta * BM);
+          tma_load_2d(st, tmA, &full[stage], 0, ta * BM);
           if (!LDGSTS) bulk_load(sf, p.sfa + (long long)ta * SF_BYTES, SF_BYTES, &full[stage]);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -436,15 +426,11 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
   }
 }
 
-// The activation maps as one kernel parameter.
-struct alignas(64) ActMaps {
-  CUtensorMap m[gemm::A_MAPS];
-};
-
 template <int MODE>
 __global__ void __launch_bounds__(gemm::THREADS, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ ActMaps tmA, GemmParams p) {
-  grouped_gemm_body<MODE>(&tmW, tmA.m, p);
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
+                        GemmParams p) {
+  grouped_gemm_body<MODE>(&tmW, &tmA, p);
 }
 
 }  // namespace k3

@@ -3,14 +3,13 @@
 // They take the reference ops' logical parameters in the reference's order (scripts/k3_moe_bmm.py:131-134,
 // 167-169: FC1 a, sf_a, b, sf_b, c, sf_c, route_map, alpha, beta, num_non_exiting, total_padded, cta_batch,
 // cta_limit; FC2 a, sf_a, b, sf_b, c, num_non_exiting, total_padded, cta_batch, cta_limit), then the GEMM's
-// shape and this build's own: `maps`, a global-memory buffer of nine TMA descriptors (the weights', then the
-// activations' with boxes of 16, 32, ..., 128 rows) that k3moe_gemm_tensor_maps fills once at load time (the
-// buffers are bound at fixed addresses, as the TRT-LLM-gen parameter block's descriptors are), and `err`, two
-// error words.
+// shape and this build's own: `maps`, a global-memory buffer of two TMA descriptors (the weights', then the
+// activations') that k3moe_gemm_tensor_maps fills once at load time (the buffers are bound at fixed
+// addresses, as the TRT-LLM-gen parameter block's descriptors are), and `err`, two error words.
 //
 //   a / sf_a   the expert weights (MXFP4, tile-major) and their tiled scales: the maps' first descriptor covers a
 //   b / sf_b   the activations: MXFP8 rows in permuted order, tile-major (kern_k3_moe_quant_permute's output,
-//              or k3moe_quant_permute's); the other descriptors cover b.  The rows are already permuted, so
+//              or k3moe_quant_permute's); the second descriptor covers b.  The rows are already permuted, so
 //              route_map is accepted for the argument list and not read.
 //   c / sf_c   FC1: MXFP8 [padded, m/2] tile-major + tiled scales; FC2: bf16 [padded, m] row-major
 //   alpha/beta FC1 with act = 1: SiTU's per-expert a, b (K3: 4 and 25, the reference's `fill_f32` carries);
@@ -26,8 +25,8 @@ namespace k3 {
 // The descriptors were written through the generic proxy (a copy into global memory): order them before the
 // tensor-map proxy's reads of this thread (the TMA producer).
 __device__ __forceinline__ void acquire_tmaps(const CUtensorMap* maps) {
-  for (int m = 0; m <= gemm::A_MAPS; ++m)
-    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps + m) : "memory");
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps) : "memory");
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(maps + 1) : "memory");
 }
 
 // The host checks of gemm_launch, made on the device (a module launch has no host code): m a multiple of 256

@@ -169,22 +169,24 @@ def test_pack_pairs_to_lands_rows_where_the_all_to_all_would(setup):
 
 
 def test_fc2_to_row_pointers_equals_fc2_to_rows(setup):
-    """FC2 storing each permuted row through a pointer table (k3moe_ep_row_ptrs over three blocks + the shared
-    block) equals FC2 storing row out_rows[r] of one buffer."""
+    """FC2 storing each permuted row through a pointer table (k3moe_ep_row_ptrs over four blocks, the last empty)
+    equals FC2 storing row out_rows[r] of one buffer.  The tables number every permuted row through exp2perm (no
+    shared expert folded in, as on the receiving rank of the expert-parallel layer, where the shared rows arrive
+    as ordinary rows): k3moe_ep_return_rows then gives every real row its number."""
     c, g, gops, oops = setup
     idx, _ = gops.topk(g["S"], g["bias"], g["rs"], K)
-    tb = k3moe.route_tables(idx, E, 0, SH)
+    tb = k3moe.route_tables(idx, E, 0, 0)
     qp, sfp = k3moe.quant_permute(g["x"], tb)
     f1q, f1sf = k3moe.fc1(g["w13"], g["w13_sf"], qp, sfp, tb, H, I, E + SH, gops.err)
     out_rows = gops.return_rows(tb, c.T, K)
     P = c.T * K
-    P_all = P + c.T
+    P_all = P
     ref = torch.zeros((P_all, H), dtype=torch.bfloat16, device=qp.device)
     k3moe._check(k3moe.lib().k3moe_fc2_to_rows(
         g["w2"].data_ptr(), g["w2_sf"].data_ptr(), f1q.data_ptr(), f1sf.data_ptr(), tb.cta_batch.data_ptr(),
         tb.cta_limit.data_ptr(), tb.meta.data_ptr(), out_rows.data_ptr(), ref.data_ptr(), H, I, E + SH, tb.cap_rows,
         tb.max_ctas, gops.err.data_ptr(), k3moe._stream()), "fc2_to_rows")
-    # the same rows split over four buffers: results [0, a), [a, b), [b, P) and the shared rows [P, P_all)
+    # the same rows split over four buffers: [0, a), [a, b), [b, P) and an empty block [P, P)
     cuts = [0, P // 3, (2 * P) // 3, P, P_all]
     bufs = [torch.zeros((cuts[i + 1] - cuts[i] + 3, H), dtype=torch.bfloat16, device=qp.device) for i in range(4)]
     sink = torch.zeros(H, dtype=torch.bfloat16, device=qp.device)

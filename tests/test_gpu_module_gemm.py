@@ -40,7 +40,7 @@ def _setup(dev, T, H, I, E, K, shared, seed):
 
 
 def _maps(mode, w, act, ne, H, I, cap, dev):
-    maps = torch.zeros(1152, dtype=torch.uint8, device=dev)  # K3MOE_GEMM_MAPS_BYTES
+    maps = torch.zeros(256, dtype=torch.uint8, device=dev)  # K3MOE_GEMM_MAPS_BYTES
     rc = k3moe.lib().k3moe_gemm_tensor_maps(mode, w.data_ptr(), act.data_ptr(), ne, H, I, cap, maps.data_ptr(),
                                             k3moe._stream())
     assert rc == 0, f"k3moe_gemm_tensor_maps = {rc}"
