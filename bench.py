@@ -946,6 +946,63 @@ def router_gemm_timing(x, wr, dev, n=20):
             "device_error_words": err[:2].tolist(), "shape": [T, Hh, E_]}
 
 
+def reference_kernels_leg(x, S, w, bias, rs, E, dev, n=20):
+    """The reference's own GEMM family on this GPU (a baseline, like the CPU leg): FlashInfer's TRT-LLM-gen MoE
+    (oracle/flashinfer_ref.py) on the same quantised operands, routed experts only (it has no shared expert),
+    tuned on this token count; beside it this build's layer without the shared expert on the same rows.  Both
+    timed with CUDA events after warm-up; their outputs compared (rel-L2)."""
+    import torch
+
+    import flashinfer_ref
+    import k3moe
+
+    if not flashinfer_ref.available():
+        return {"unavailable": "FlashInfer's TRT-LLM-gen launcher is not prebuilt (make -C oracle flashinfer)"}
+    T = x.shape[0]
+    ne = E * 2 * I
+    mine = k3moe.MoELayer(H, I, E, K, 0, w["w13"], w["w13_sf"], w["w2"], w["w2_sf"], bias, rs, max_tokens=T,
+                          device=dev)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    ms_mine = timed(lambda: mine.forward(S, x, out))
+    off = mine.offsets(T)
+    idx = mine.ws[off["idx"]:off["idx"] + T * K * 4].view(torch.int32).view(T, K).clone()
+    wts = mine.ws[off["wts"]:off["wts"] + T * K * 4].view(torch.float32).view(T, K).clone()
+    kg4 = H // 128
+    ref = flashinfer_ref.ReferenceMoE(w["w13"][:ne], w["w13_sf"][:ne // 128 * kg4 * 512], w["w2"][:E * H],
+                                      w["w2_sf"][:E * H // 128 * (I // 128) * 512], E, H, I, K)
+    q, sf = k3moe.quant_mxfp8(x, tiled_sf=False)
+    qf = q.view(torch.float8_e4m3fn)
+    tk = flashinfer_ref.pack_topk(idx, wts)
+    ref.tune(qf, sf, tk)
+    ms_ref = timed(lambda: ref.forward(qf, sf, tk, finalize=True, tune_max=T))
+    ms_quant = timed(lambda: k3moe.quant_mxfp8(x, tiled_sf=False))
+    y = ref.forward(qf, sf, tk, finalize=True, tune_max=T)
+    torch.cuda.synchronize()
+    rel = float((out.float() - y.float()).norm() / y.float().norm())
+    del ref, mine
+    torch.cuda.empty_cache()
+    return {"flashinfer_trtllm_gen_ms": ms_ref, "flashinfer_input_quant_ms": ms_quant,
+            "k3moe_routed_layer_ms": ms_mine, "vs_reference_kernels": (ms_ref + ms_quant) / ms_mine,
+            "output_rel_l2": rel,
+            "what": "routed experts only (no shared expert), the same rows, routing and quantised operands; "
+                    "FlashInfer 0.6.11 trtllm_fp4_block_scale_routed_moe (routing from the given top-k, FC1, FC2, "
+                    "finalize), tuned on this token count, plus its input MXFP8 quantisation; k3moe: the whole "
+                    "layer (top-k, tables, permute, FC1, FC2, combine)"}
+
+
 TRAFFIC_SOURCE = ("ncu DRAM bytes (read + write) per algorithmic byte of FC1 on the small-case capture "
                   "(profiles/grouped_gemm_fc1_fc2_small_case.md), times this launch's algorithmic bytes")
 
@@ -987,6 +1044,8 @@ def main():
                     help="N > 1: FC2 in this many column slices, each returned by its own all-to-all beside the next")
     ap.add_argument("--ep-fc2-cap", type=int, default=0,
                     help="N > 1 with --ep-overlap > 1: FC2's persistent blocks (0: one an SM), SMs left to NCCL")
+    ap.add_argument("--no-reference-kernels", action="store_true",
+                    help="skip the leg that times the reference's GEMM family (FlashInfer TRT-LLM-gen) on this GPU")
     ap.add_argument("--ep-transport", default="nccl", choices=["nccl", "peer"],
                     help="N > 1: the two all-to-alls over NCCL, or stores into the peers' buffers over NVLink")
     ap.add_argument("--native", action="store_true",
@@ -1111,6 +1170,13 @@ def main():
     # ---------------- the router GEMM (the step before the path, outside the layer's time): this build's
     # tcgen05 kernel against cuBLAS (torch.mm, bf16 out) on the same x and W_router (bf16)
     router = router_gemm_timing(x, hin["w_router"], dev)
+    refk = None
+    if not args.no_reference_kernels:
+        try:
+            refk = reference_kernels_leg(x, S, {"w13": w13, "w13_sf": w13_sf, "w2": w2, "w2_sf": w2_sf}, bias, rs,
+                                         E, dev)
+        except Exception as ex:  # the baseline may not load here: the line says why
+            refk = {"unavailable": f"{type(ex).__name__}: {str(ex)[:200]}"}
 
     # ---------------- the CPU leg (after timing): the oracle checks this run's own intermediates on sampled
     # token tiles and every row's routing, and its FC1 + FC2 time over the sample is the CPU baseline
@@ -1152,6 +1218,7 @@ def main():
                           "neighbouring steps' compute (double buffers)"},
         "gpu_launches": 8 * args.steps,
         "router_gemm": router,
+        "reference_kernels": refk,
         "gemm_trace": gemm_trace,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,

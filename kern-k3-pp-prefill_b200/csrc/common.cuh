@@ -65,19 +65,15 @@ __device__ __forceinline__ int mx8_exponent(float amax) {
   return min(max(e, -127), 127);
 }
 
-// The same exponent by exact arithmetic on the f32 quotient q = amax / 448
-// (IEEE division): the exponent of q, plus one unless q is a power of two.
-// Used where no reference rounding chain must be mirrored (FC1's output).
-__device__ __forceinline__ int mx8_exponent_exact(float amax) {
-  if (!(amax > 0.f)) return 0;
-  const u32 b = __float_as_uint(__fdiv_rn(amax, 448.f));
-  int e;
-  if ((b >> 23) != 0) {
-    e = (int)(b >> 23) - 127 + ((b & 0x7fffffu) ? 1 : 0);
-  } else {  // subnormal quotient: below 2^-126, clamped anyway
-    e = -127;
-  }
-  return min(max(e, -127), 127);
+// The block exponent of FC1's output requantisation: the OCP MX rule, e = floor(log2(amax)) - 8 (E4M3's largest
+// power of two is 2^8), clamped to [-127, 127]; the scaled group's largest values then lie in [256, 512) and
+// the conversion saturates them at 448.  This is the rule of the reference's FC1 (the TRT-LLM-gen batched GEMM
+// family): an fp32 restatement with it reproduces that GEMM's outputs on the same operands to 5e-5 rel-L2,
+// where ceil(log2(amax / 448)) (the activation quantiser's rule) leaves 2.5%.  Exact: floor(log2(amax)) is the
+// unbiased exponent field of a normal f32; zero and subnormal amax give -127.
+__device__ __forceinline__ int mx8_exponent_ocp(float amax) {
+  const int eb = (int)((__float_as_uint(amax) >> 23) & 0xffu);
+  return min(max(eb - 127 - 8, -127), 127);
 }
 
 // 2^n as an f32 built from its bits, n in [-126, 127]

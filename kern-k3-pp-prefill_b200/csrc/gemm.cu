@@ -377,7 +377,7 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
               hv[j] = gated_act(gf, uf, p.act, ga, gra, gb, grb);
               amax = fmaxf(amax, fabsf(hv[j]));
             }
-            const int e = mx8_exponent_exact(amax);
+            const int e = mx8_exponent_ocp(amax);
             const float s = pow2_normal(-e);
             u32 q[8];
 #pragma unroll

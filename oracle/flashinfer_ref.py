@@ -12,13 +12,31 @@ Weights go in as the reference binds them: the checkpoint form (row-major E2M1 r
 [w3 (up); w1 (gate)]) through the reference's load-time shuffles (source/k3_moe_prefill.cu:237-259: within
 32 rows, row r takes row (r/32)*32 + (r%8)*4 + (r%32)/8; FC1 interleaves the two halves; scales 128x4-tiled an
 expert), restated here with torch indexing on the device.  The host launcher of that FlashInfer module is
-compiled on first use (FlashInfer's JIT; FLASHINFER_WORKSPACE_BASE picks the cache directory).
+compiled once into oracle/_fi (`make -C oracle flashinfer`, FlashInfer's JIT with FLASHINFER_WORKSPACE_BASE set
+there).  What this pinned: the reference FC1 requantises its output with the OCP MX exponent rule
+(floor(log2(amax)) - 8), which the oracle's and k3moe's FC1 now use too.
 
-Only bench.py's reference-kernel leg and tests/ import this; the product never does.
+Only bench.py's baseline legs and tests/ import this; the product never does.
 """
 from __future__ import annotations
 
+import glob
+import os
+
 import torch
+
+FI_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_fi")
+
+
+def available() -> bool:
+    """FlashInfer's host launcher of the TRT-LLM-gen MoE has been compiled into oracle/_fi (make -C oracle
+    flashinfer): without it the first call would compile it (about 20 minutes), so callers skip instead."""
+    return bool(glob.glob(os.path.join(FI_DIR, ".cache", "flashinfer", "*", "*", "cached_ops",
+                                       "fused_moe_trtllm_sm100", "fused_moe_trtllm_sm100.so")))
+
+
+def _use_cache():
+    os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", FI_DIR)
 
 
 def _shuffle_rows(n: int, gated: bool, device) -> torch.Tensor:
@@ -79,6 +97,7 @@ class ReferenceMoE:
     """The routed experts (no shared expert) through FlashInfer's TRT-LLM-gen MoE."""
 
     def __init__(self, w13, w13_sf, w2, w2_sf, E, H, I, K):
+        _use_cache()
         import flashinfer.fused_moe as fm
 
         self.fm = fm
@@ -90,7 +109,22 @@ class ReferenceMoE:
         """q_fp8 [T, H] float8_e4m3fn, sf_linear [T, H/32] (UE8M0 bytes), topk_packed [T, K] int32.
         finalize: the combined bf16 output [T, H]; else (FC2 rows [padded, H], expanded->permuted row map)."""
         out = self.fm.trtllm_fp4_block_scale_routed_moe(
-            topk_packed, None, q_fp8, sf_linear.view(torch.float8_e4m3fn), self.g1, self.g1s, None, None, None, None, self.g2, self.g2s,
-            None, None, None, None, self.E, self.K, None, None, self.I, 0, self.E, None,
+            topk_packed, None, q_fp8, sf_linear.view(torch.float8_e4m3fn), self.g1, self.g1s, None, None, None,
+            None, self.g2, self.g2s, None, None, None, None, self.E, self.K, None, None, self.I, 0, self.E, None,
             routing_method_type=1, do_finalize=finalize, tune_max_num_tokens=tune_max)
         return out[0] if finalize else (out[0], out[2])
+
+    def tune(self, q_fp8, sf_linear, topk_packed):
+        """FlashInfer's autotuner over this call's token count only (its default sweep of 1..8192 tokens took
+        over 20 minutes at the K3 shape)."""
+        import flashinfer
+        import flashinfer.fused_moe.core as fcore
+
+        T = q_fp8.shape[0]
+        orig = fcore.get_hybrid_num_tokens_buckets
+        fcore.get_hybrid_num_tokens_buckets = lambda mx, mn=1: (T,)
+        try:
+            with flashinfer.autotune(True):
+                self.forward(q_fp8, sf_linear, topk_packed, finalize=True, tune_max=T)
+        finally:
+            fcore.get_hybrid_num_tokens_buckets = orig

@@ -25,6 +25,7 @@ uint8_t orc_f32_to_e4m3_sat(float f);        /* RNE, saturate to +-448, NaN -> 0
 float orc_e4m3_to_f32(uint8_t b);
 float orc_e2m1_to_f32(uint8_t nibble);
 int orc_mx8_exponent(float amax);            /* ceil(log2(amax/448)) clamped, 0 for amax 0 */
+int orc_mx8_exponent_ocp(float amax);        /* FC1's output: floor(log2(amax)) - 8 clamped, -127 for 0 */
 long long orc_sf_tiled_offset(long long r, int kb, int kg4);
 /* tile-major GEMM operands (128 x 128-element tiles, tile (r/128, k/128) at
  * index (r/128)*(K/128) + k/128, row-major inside): byte of E4M3 element (r, k),
@@ -56,8 +57,11 @@ void orc_combine(const uint16_t* fc2, const int32_t* exp2perm, const float* wts,
                  int ldo, int T, int out_rows, int K, int cols);
 
 /* FC1 / FC2 over the tables: fp32 dequantise-and-matmul of the same quantised
- * operands (no reference code: the reference GEMMs are closed cubins).
- * Rows of tiles c in [c0, c1) only.  fc1: SwiGLU then the MXFP8 rule. */
+ * operands (the reference GEMMs are closed cubins; their family, run through
+ * FlashInfer's TRT-LLM-gen MoE on the same operands, pins this restatement:
+ * oracle/flashinfer_ref.py, tests/test_gpu_flashinfer_ref.py).
+ * Rows of tiles c in [c0, c1) only.  fc1: the gate, then MXFP8 with the OCP
+ * exponent rule (orc_mx8_exponent_ocp), the reference FC1's. */
 void orc_fc1(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_perm, const uint8_t* sf_perm,
              const int32_t* cta_batch, const int32_t* cta_limit, int c0, int c1, int H, int I, uint8_t* fc1_q,
              uint8_t* fc1_sf);

@@ -76,6 +76,18 @@ int orc_mx8_exponent(float amax) {
   return e;
 }
 
+/* FC1's output rule (the reference's TRT-LLM-gen FC1): OCP MX, e = floor(log2(amax)) - 8, clamped; zero and
+ * subnormal amax give -127.  frexp: amax = m 2^ex with m in [0.5, 1), so floor(log2(amax)) = ex - 1. */
+int orc_mx8_exponent_ocp(float amax) {
+  if (!(amax >= 1.17549435e-38f)) return -127;
+  int ex;
+  frexpf(amax, &ex);
+  int e = ex - 1 - 8;
+  if (e < -127) e = -127;
+  if (e > 127) e = 127;
+  return e;
+}
+
 long long orc_sf_tiled_offset(long long r, int kb, int kg4) {
   return ((r / 128) * kg4 + kb / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + kb % 4;
 }

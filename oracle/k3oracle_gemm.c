@@ -97,7 +97,7 @@ void orc_fc1_act(const uint8_t* w13, const uint8_t* w13_sf, const uint8_t* q_per
           const float a = fabsf(h[(size_t)j * I + kb * 32 + i]);
           if (a > amax) amax = a;
         }
-        const int ex = orc_mx8_exponent(amax);
+        const int ex = orc_mx8_exponent_ocp(amax);
         const float s = ldexpf(1.0f, -ex);
         uint8_t* grp = fc1_q + orc_op8_offset(row0 + j, kb * 32, I);
         for (int i = 0; i < 32; ++i) grp[i] = orc_f32_to_e4m3_sat(h[(size_t)j * I + kb * 32 + i] * s);

@@ -26,6 +26,8 @@ def lib():
         _lib = ctypes.CDLL(LIB)
         _lib.orc_mx8_exponent.restype = ctypes.c_int
         _lib.orc_mx8_exponent.argtypes = [ctypes.c_float]
+        _lib.orc_mx8_exponent_ocp.restype = ctypes.c_int
+        _lib.orc_mx8_exponent_ocp.argtypes = [ctypes.c_float]
         _lib.orc_f32_to_e4m3_sat.restype = ctypes.c_uint8
         _lib.orc_f32_to_e4m3_sat.argtypes = [ctypes.c_float]
         _lib.orc_e4m3_to_f32.restype = ctypes.c_float

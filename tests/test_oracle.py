@@ -181,3 +181,19 @@ def test_zipf_bias_shapes_routing():
     _, _, kl0 = cases.zipf_bias(S, 8, betas=[0.0])
     assert beta > 0 and kl < kl0
     assert (h == 0).sum() >= 3 and h.max() > 8 * h.mean()
+
+
+def test_mx8_exponent_ocp_every_bf16_amax():
+    """FC1's output rule (the reference FC1's): e = floor(log2(amax)) - 8, clamped; -127 for zero."""
+    lib = oracle.lib()
+    bits = np.arange(1, 0x7F80, dtype=np.uint32)
+    amax = oracle.bf16_to_f32(bits.astype(np.uint16))[::5]
+    got = np.array([lib.orc_mx8_exponent_ocp(float(a)) for a in amax])
+    want = np.clip(np.floor(np.log2(amax.astype(np.float64))) - 8, -127, 127).astype(np.int64)
+    want[amax < 1.17549435e-38] = -127
+    assert np.array_equal(got, want)
+    assert lib.orc_mx8_exponent_ocp(0.0) == -127
+    # the largest scaled value lies in [256, 512): the top of a group saturates at 448 more often than it rounds
+    for a in (1.0, 1.75, 3.0, 500.0, 2.0 ** -60):
+        e = lib.orc_mx8_exponent_ocp(a)
+        assert 256.0 <= a * 2.0 ** -e < 512.0
