@@ -556,15 +556,23 @@ def run_ep(args, world, rank, dev):
     x, S, bias, rs = device_inputs(host_inputs(T, E, 1000 + rank), dev)
     owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
     w = rank_weights(E, mine, dev)
-    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, owner=owner,
-                                overlap_chunks=args.ep_overlap, fc2_grid_cap=args.ep_fc2_cap,
-                                transport=args.ep_transport, max_tokens=T if args.ep_transport == "peer" else None)
+    device_step = args.ep_transport == "device"
+    if device_step:
+        layer = k3moe_ep.DeviceEPMoELayer(H, I, E, K, SHARED, w, bias, rs, max_tokens=T, owner=owner, device=dev)
+    else:
+        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, owner=owner,
+                                    overlap_chunks=args.ep_overlap, fc2_grid_cap=args.ep_fc2_cap,
+                                    transport=args.ep_transport,
+                                    max_tokens=T if args.ep_transport == "peer" else None)
     for _ in range(args.warmup):
         layer.forward(S, x)
     torch.cuda.synchronize()
     names = ("dispatch", "fc1", "combine")
-    evs = [{n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
-           for _ in range(args.steps)]
+    if device_step:  # the step's 8 stage events, read as the same three intervals
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(args.steps)]
+    else:
+        evs = [{n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
+               for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()
     torch.cuda.synchronize()
@@ -577,7 +585,11 @@ def run_ep(args, world, rank, dev):
         torch.cuda.synchronize()
     dist.barrier()
     ms = start.elapsed_time(stop) / args.steps
-    part = {n: float(np.mean([e[n][0].elapsed_time(e[n][1]) for e in evs])) for n in names}
+    if device_step:  # dispatch: pack + exchange; fc1; combine: FC2's end to every peer's results in
+        spans = {"dispatch": (1, 2), "fc1": (3, 4), "combine": (5, 6)}
+        part = {n: float(np.mean([e[a].elapsed_time(e[b]) for e in evs])) for n, (a, b) in spans.items()}
+    else:
+        part = {n: float(np.mean([e[n][0].elapsed_time(e[n][1]) for e in evs])) for n in names}
     t = torch.tensor([ms, part["dispatch"], part["combine"], part["fc1"]], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, disp_ms, comb_ms, fc1_ms = [float(v) for v in t.tolist()]
@@ -590,8 +602,7 @@ def run_ep(args, world, rank, dev):
     t = torch.tensor([e2e_ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
-    tb = layer.last["tables"]
-    counts = tb.counts.cpu().numpy()
+    counts = (layer.expert_rows() if device_step else layer.last["tables"].counts).cpu().numpy()
     routed_rows, touched = int(counts.sum()), int((counts > 0).sum())
     fc1_bytes = touched * (2 * I * H // 2 + 2 * I * H // 32) + routed_rows * (H + H // 32 + I + I // 32)
     # ---------------- the check (untimed): this rank's rows through the 1-GPU layer over all 896 experts
@@ -601,7 +612,8 @@ def run_ep(args, world, rank, dev):
     out_1 = full.forward(S, x)
     torch.cuda.synchronize()
     full.check_device_error(T)
-    words = layer.ops.err[:2].tolist()  # the transport's bounded waits and table checks
+    # the transport's bounded waits and table checks
+    words = list(layer.error_words()[1]) if device_step else layer.ops.err[:2].tolist()
     same = torch.tensor([1 if torch.equal(out_ep.view(torch.int16), out_1.view(torch.int16)) and words == [0, 0]
                          else 0], device=dev)
     dist.all_reduce(same, op=dist.ReduceOp.MIN)
@@ -633,9 +645,12 @@ def run_ep(args, world, rank, dev):
                     "d2h_bytes_per_step": int(x.numel() * 2) * world,
                     "copies": "every step's x, S in and output back over PCIe, on side streams overlapping the "
                               "neighbouring steps' compute (double buffers)"},
-            # topk, 2 x 3 plan launches, pairs, pack, shared pack, ids, 3 table launches, unpack, return rows,
-            # FC1, FC2 (a launch a slice), combine
-            "gpu_launches": (18 + args.ep_overlap + (4 if args.ep_transport == "peer" else 0)) * args.steps,
+            # nccl / peer: topk, 2 x 3 plan launches, pairs, pack, shared pack, ids, 3 table launches, unpack,
+            # return rows, FC1, FC2 (a launch a slice), combine (+ peer: row pointers, 2 signals, 2 waits);
+            # device: topk, plan, pack, exchange, ids, 3 table launches, unpack, FC1, row pointers, FC2,
+            # exchange, combine
+            "gpu_launches": (14 if device_step else
+                             18 + args.ep_overlap + (4 if args.ep_transport == "peer" else 0)) * args.steps,
             "decode": dec,
             "clocks": clk.summary(),
             "cpu_baseline": None,
@@ -665,7 +680,11 @@ def decode_pass(args, world, rank, dev, w, owner, full):
     T = Tall // world
     x_all, S_all, bias, rs = device_inputs(host_inputs(Tall, E, 2000), dev)
     x, S = x_all[rank * T:(rank + 1) * T].contiguous(), S_all[rank * T:(rank + 1) * T].contiguous()
-    layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
+    device_step = args.ep_transport == "device"
+    if device_step:
+        layer = k3moe_ep.DeviceEPMoELayer(H, I, E, K, SHARED, w, bias, rs, max_tokens=T, owner=owner, device=dev)
+    else:
+        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
     run = lambda: layer.forward(S, x)  # noqa: E731
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -695,11 +714,18 @@ def decode_pass(args, world, rank, dev, w, owner, full):
     eager_us = timed(run)
     # eager breakdown: the dispatch all-to-all, the expert GEMMs (tables .. FC2), the combine all-to-all
     names = ("dispatch", "ffn", "combine")
-    ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
     dist.barrier()
-    layer.forward(S, x, ev)
-    torch.cuda.synchronize()
-    stage_us = {n: round(mx(ev[n][0].elapsed_time(ev[n][1]) * 1e3), 1) for n in names}
+    if device_step:  # dispatch: plans + pack + exchange; ffn: tables .. FC2; combine: exchange + combine
+        ev8 = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        layer.forward(S, x, events=ev8)
+        torch.cuda.synchronize()
+        spans = {"dispatch": (0, 2), "ffn": (2, 5), "combine": (5, 7)}
+        stage_us = {n: round(mx(ev8[a].elapsed_time(ev8[b]) * 1e3), 1) for n, (a, b) in spans.items()}
+    else:
+        ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in names}
+        layer.forward(S, x, ev)
+        torch.cuda.synchronize()
+        stage_us = {n: round(mx(ev[n][0].elapsed_time(ev[n][1]) * 1e3), 1) for n in names}
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         static_out = run()
@@ -712,14 +738,18 @@ def decode_pass(args, world, rank, dev, w, owner, full):
     torch.cuda.synchronize()
     same = torch.tensor([1 if torch.equal(static_out.view(torch.int16), ref.view(torch.int16)) else 0], device=dev)
     dist.all_reduce(same, op=dist.ReduceOp.MIN)
-    counts = layer.last["tables"].counts.cpu().numpy()
+    counts = (layer.expert_rows() if device_step else layer.last["tables"].counts).cpu().numpy()
     per_expert = 2 * I * H // 2 + 2 * I * H // 32 + H * I // 2 + H * I // 32
     wbytes = mx(float(int((counts > 0).sum()) * per_expert))
     hbm_peak, _ = peaks()
     graph.reset()
     del graph
     torch.cuda.synchronize()
+    if device_step:
+        dist.barrier()  # every rank's last step done before the peers' buffers are unmapped
+        layer.close()
     return {"us": us, "eager_us": eager_us, "graph": True, "tokens": Tall, "tokens_per_gpu": T,
+            "transport": args.ep_transport,
             "stage_us_eager": stage_us, "bit_identical_to_1gpu": bool(same.item() == 1),
             "roofline": {"bound": "hbm", "bytes_slowest_rank": wbytes,
                          "frac": wbytes / (us / 1e6) / 1e9 / hbm_peak}}
@@ -747,7 +777,11 @@ def run_decode(args, world, rank, dev):
     else:
         owner, mine = rank_experts(E, world, rank, bias, args.ep_placement)
         w = rank_weights(E, mine, dev)
-        layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
+        if args.ep_transport == "device":
+            layer = k3moe_ep.DeviceEPMoELayer(H, I, E, K, SHARED, w, bias, rs, max_tokens=T, owner=owner,
+                                              device=dev)
+        else:
+            layer = k3moe_ep.EPMoELayer(H, I, E, K, SHARED, w, bias, rs, device=dev, fixed_tokens=T, owner=owner)
         run = lambda: layer.forward(S, x)  # noqa: E731
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -806,6 +840,8 @@ def run_decode(args, world, rank, dev):
     if world == 1:
         off = layer.offsets(T)
         counts = layer.ws[off["counts"]:off["counts"] + 4 * (E + SHARED)].view(torch.int32).cpu().numpy()
+    elif args.ep_transport == "device":
+        counts = layer.expert_rows().cpu().numpy()
     else:
         counts = layer.last["tables"].counts.cpu().numpy()
     touched = int((counts > 0).sum())
@@ -821,6 +857,7 @@ def run_decode(args, world, rank, dev):
             "config": {"workload": "K3-shape decode MoE step (config 2)", "tokens": Tall, "tokens_per_gpu": T,
                        "H": H, "I": I, "E": E, "E_per_gpu": El, "K": K, "shared_expert_width": I, "rs": RS,
                        "parallelism": f"ep{world}", "expert_placement": args.ep_placement if world > 1 else None,
+                       "transport": args.ep_transport if world > 1 else None,
                        "l2": "inputs larger than L2: each step streams the touched experts' weights"},
             "roofline": {"kernel": "whole decode layer (weights of the touched experts, slowest rank)",
                          "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -841,6 +878,9 @@ def run_decode(args, world, rank, dev):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+        if args.ep_transport == "device":
+            layer.close()
+            dist.barrier()
         dist.destroy_process_group()
 
 
@@ -1046,8 +1086,10 @@ def main():
                     help="N > 1 with --ep-overlap > 1: FC2's persistent blocks (0: one an SM), SMs left to NCCL")
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip the leg that times the reference's GEMM family (FlashInfer TRT-LLM-gen) on this GPU")
-    ap.add_argument("--ep-transport", default="nccl", choices=["nccl", "peer"],
-                    help="N > 1: the two all-to-alls over NCCL, or stores into the peers' buffers over NVLink")
+    ap.add_argument("--ep-transport", default="nccl", choices=["nccl", "peer", "device"],
+                    help="N > 1: the two all-to-alls over NCCL; stores into the peers' buffers over NVLink after "
+                         "a counts exchange (peer); or the device-resident step, one C-ABI call with fixed peer "
+                         "regions and no host synchronisation (device)")
     ap.add_argument("--native", action="store_true",
                     help="the layer at the reference's own K3 shapes (latent 3584, I 3072, top-16, SiTU), N = 1")
     args = ap.parse_args()

@@ -347,6 +347,65 @@ int k3moe_layer_forward_events(const k3moe_layer_args* a, void* workspace, size_
  * err (14 entries). */
 int k3moe_layer_workspace_offsets(int T, int H, int I, int E, int K, int shared, size_t* offsets14);
 
+/* ---------------------------------------------------------------- the expert-parallel layer, device-resident
+ * One rank's part of an expert-parallel MoE layer over peer memory (NVLink / NVSwitch), as one call that
+ * enqueues the whole step and never synchronises with the host: top-k -> the sender's plans -> MXFP8 pack
+ * stored straight into the destinations' receive buffers -> a flag exchange -> tables -> FC1 -> FC2 storing
+ * each result row into its owner's return buffer -> a flag exchange -> the owner's combine.  Every rank's
+ * receive buffer has a fixed region a source rank (max_tokens rows), so a rank needs no other rank's counts
+ * before it sends; the whole step can be captured in a CUDA graph.  The output is the bytes of
+ * k3moe_layer_forward over all ranks' experts (same arithmetic, same summation order).
+ * Each rank holds E / world routed experts (owner: host int32 [E], the rank of each expert, E / world each, a
+ * rank's experts in increasing id order being its local experts 0, 1, ...; NULL: contiguous blocks) and, with
+ * shared, a replica of the shared expert as local expert E / world of its weight tensors.
+ * Set-up, on every rank: allocate k3moe_ep_peer_bytes (zeroed, 256-byte aligned) and
+ * k3moe_ep_workspace_bytes; export the peer buffer (k3moe_ipc_export), exchange the handles, import the
+ * peers' (k3moe_ipc_import); k3moe_ep_create; then a host barrier across the ranks before any rank's first
+ * k3moe_ep_forward (create clears this rank's flags).  Every rank calls k3moe_ep_forward the same number of
+ * times.  A peer that stays late past wait_budget_ns is recorded in the error words (k3moe_ep_errors; bit 0,
+ * site 0xA00 + 0x10 * phase + rank) and the step completes with what arrived; nothing traps.  world <= 16.
+ * No counterpart in the reference for the MoE (its decode EP replicates the batch and all-reduces,
+ * roofline/decode.md:164-166; its fused all-reduce + finalize kern_k3_ar_finalize_rms,
+ * source/k3_ar_fused.cu:916, is the combine-with-collective this step's FC2 epilogue stores replace). */
+typedef struct k3moe_ep_config {
+  int world, rank;
+  int H, I;                 /* multiples of 256 */
+  int E, K;                 /* routed experts in all (E % world == 0, E <= 1024), top-k (a power of 2, <= 16) */
+  int shared;               /* 1: local expert E / world is the always-on shared expert */
+  int max_tokens;           /* tokens a rank per call (T <= max_tokens) */
+  int activation;           /* FC1 gate: K3MOE_ACT_SWIGLU (0) or K3MOE_ACT_SITU (1) */
+  uint64_t wait_budget_ns;  /* bound of each flag wait (0: 5 s) */
+} k3moe_ep_config;
+typedef struct k3moe_ep k3moe_ep;
+
+size_t k3moe_ep_peer_bytes(const k3moe_ep_config* c);
+size_t k3moe_ep_workspace_bytes(const k3moe_ep_config* c);
+/* peer_bases: host array [world], every rank's peer buffer as mapped in this process ([rank] = peer_buffer).
+ * Weights: this rank's experts, tile-major as above. */
+int k3moe_ep_create(const k3moe_ep_config* c, const int32_t* owner, const uint8_t* w13, const uint8_t* w13_sf,
+                    const uint8_t* w2, const uint8_t* w2_sf, void* peer_buffer, const uint64_t* peer_bases,
+                    void* workspace, size_t ws_bytes, k3moe_stream_t stream, k3moe_ep** out);
+/* One step over this rank's T tokens: S f32 [T, lds] router logits (E wide), bias f32 [E], rs bf16 [1],
+ * x bf16 [T, ldx], out bf16 [T, ldo]. */
+int k3moe_ep_forward(k3moe_ep* ep, const float* S, int lds, const float* bias, const void* rs_bf16,
+                     const void* x_bf16, int ldx, int T, void* out_bf16, int ldo, k3moe_stream_t stream);
+/* The same call recording CUDA events (may be null) on `stream`: [0] start, [1] after top-k and the plans,
+ * [2] after the dispatch (pack + exchange), [3] after tables + unpack, [4] after FC1, [5] after FC2, [6] after
+ * the combine exchange, [7] after the combine (n_events <= 8 used). */
+int k3moe_ep_forward_events(k3moe_ep* ep, const float* S, int lds, const float* bias, const void* rs_bf16,
+                            const void* x_bf16, int ldx, int T, void* out_bf16, int ldo, k3moe_stream_t stream,
+                            void* const* events, int n_events);
+/* The step's device error words (two u32, for k3moe_read_error); the rows received in the last step
+ * (counts, W + 1 u32 device words: per source rank, then this rank's shared rows). */
+uint32_t* k3moe_ep_errors(k3moe_ep* ep);
+const uint32_t* k3moe_ep_counts(k3moe_ep* ep);
+/* The last step's routing tables on this rank: rows routed to each local expert (E / world + shared int32
+ * device words) and meta (num_non_exiting, total_padded, ...: 4 int32 device words). */
+const int32_t* k3moe_ep_expert_rows(k3moe_ep* ep);
+const int32_t* k3moe_ep_meta(k3moe_ep* ep);
+/* Frees the host object only (the caller owns every buffer). */
+void k3moe_ep_destroy(k3moe_ep* ep);
+
 /* Tracing: with a device buffer of 32 zeroed u64 set, every later FC1 / FC2
  * launch of this process adds per-role SM cycle counters into it (FC1 at
  * [0..15], FC2 at [16..31]): [0] producer cycles, [1] producer cycles waiting

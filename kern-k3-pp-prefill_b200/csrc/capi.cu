@@ -5,12 +5,14 @@
 
 #include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "../../include/k3moe.h"
 #include "gemm.cu"
 #include "route.cu"
 #include "ep.cu"
 #include "ep_peer.cu"
+#include "ep_device.cu"
 #include "router.cu"
 #include "dropin.cu"
 
@@ -749,6 +751,288 @@ int k3moe_read_error(uint32_t* err, uint32_t* out2, int clear, k3moe_stream_t st
   if (cudaStreamSynchronize(s) != cudaSuccess) return K3MOE_ELAUNCH;
   return (out2[0] | out2[1]) ? K3MOE_EDEVICE : K3MOE_OK;
 }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- the device-resident expert-parallel step
+namespace {
+
+struct EpPeerLayout {
+  long long stride, back_col, recv_off, back_off, counts_off, flags_off, total;
+};
+
+EpPeerLayout ep_peer_layout(const k3moe_ep_config& c) {
+  EpPeerLayout L;
+  L.back_col = (long long)c.H + c.H / 32 + 2LL * c.K;
+  L.stride = (L.back_col + 4 + 15) / 16 * 16;
+  L.recv_off = 0;
+  L.back_off = (long long)align_up((size_t)(c.world + 1) * c.max_tokens * L.stride, 256);
+  L.counts_off = L.back_off + (long long)align_up((size_t)c.max_tokens * c.K * c.H * 2, 256);
+  L.flags_off = L.counts_off + 256;
+  L.total = L.flags_off + 256;
+  return L;
+}
+
+enum { EW_EPOCH, EW_ERR, EW_OWNER, EW_LOCAL, EW_IDX, EW_WTS, EW_DEST, EW_LID, EW_SEND_POS, EW_PAIR_POS, EW_PAIR_BACK,
+       EW_ROWS_TO, EW_IDS, EW_COUNTS, EW_CTA_BATCH, EW_CTA_LIMIT, EW_META, EW_ROUTE_MAP, EW_EXP2PERM, EW_SCRATCH,
+       EW_QP, EW_SFP, EW_FC1Q, EW_FC1SF, EW_PTRS, EW_SHARED, EW_N };
+
+struct EpWsLayout {
+  size_t off[EW_N];
+  size_t total;
+  int El, nexp, R_all, max_ctas, cap_rows;
+};
+
+EpWsLayout ep_ws_layout(const k3moe_ep_config& c) {
+  EpWsLayout L;
+  const int W = c.world, T = c.max_tokens, K = c.K;
+  L.El = c.E / W;
+  L.nexp = L.El + (c.shared ? 1 : 0);
+  L.R_all = (W + 1) * T;
+  // permuted rows: the picks a rank can receive (every source's every pick, at most one a local expert) and
+  // its own shared rows, padded to 128 an expert
+  const long long picks = (long long)W * T * std::min(K, L.El) + (c.shared ? T : 0);
+  L.max_ctas = (int)(L.nexp + cdiv(picks, 128));
+  L.cap_rows = L.max_ctas * 128;
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = at;
+    at = align_up(at + bytes, 1024);
+    return o;
+  };
+  L.off[EW_EPOCH] = take(16);
+  L.off[EW_ERR] = take(16);
+  L.off[EW_OWNER] = take((size_t)c.E * 4);
+  L.off[EW_LOCAL] = take((size_t)c.E * 4);
+  L.off[EW_IDX] = take((size_t)T * K * 4);
+  L.off[EW_WTS] = take((size_t)T * K * 4);
+  L.off[EW_DEST] = take((size_t)T * K * 4);
+  L.off[EW_LID] = take((size_t)T * K * 4);
+  L.off[EW_SEND_POS] = take((size_t)T * K * 4);
+  L.off[EW_PAIR_POS] = take((size_t)T * W * 4);
+  L.off[EW_PAIR_BACK] = take((size_t)T * W * 4);
+  L.off[EW_ROWS_TO] = take((size_t)(W + 1) * 4);
+  L.off[EW_IDS] = take((size_t)L.R_all * K * 4);
+  L.off[EW_COUNTS] = take((size_t)L.nexp * 4);
+  L.off[EW_CTA_BATCH] = take((size_t)L.max_ctas * 4);
+  L.off[EW_CTA_LIMIT] = take((size_t)L.max_ctas * 4);
+  L.off[EW_META] = take(16);
+  L.off[EW_ROUTE_MAP] = take((size_t)L.cap_rows * 4);
+  L.off[EW_EXP2PERM] = take((size_t)L.R_all * K * 4);
+  L.off[EW_SCRATCH] = take(k3moe_route_scratch_bytes(L.R_all, L.nexp, 0));
+  L.off[EW_QP] = take((size_t)L.cap_rows * c.H);
+  L.off[EW_SFP] = take((size_t)L.cap_rows * c.H / 32);
+  L.off[EW_FC1Q] = take((size_t)L.cap_rows * c.I);
+  L.off[EW_FC1SF] = take((size_t)L.cap_rows * c.I / 32);
+  L.off[EW_PTRS] = take((size_t)L.cap_rows * 8);
+  L.off[EW_SHARED] = take((size_t)(T + 1) * c.H * 2);  // the last row: the sink of a bad return index
+  L.total = at;
+  return L;
+}
+
+bool ep_config_ok(const k3moe_ep_config* c) {
+  return c && c->world >= 1 && c->world <= EP_MAX_RANKS && c->rank >= 0 && c->rank < c->world && c->H > 0 &&
+         c->H % 256 == 0 && c->I > 0 && c->I % 256 == 0 && c->E >= 1 && c->E <= 1024 && c->E % c->world == 0 &&
+         c->K >= 1 && c->K <= 16 && (c->K & (c->K - 1)) == 0 && c->K <= c->E && c->max_tokens >= 1 &&
+         c->max_tokens <= 65536 && (c->activation == 0 || c->activation == 1) &&
+         (long long)(c->world + 1) * c->max_tokens * c->K < (1LL << 31);
+}
+
+}  // namespace
+
+struct k3moe_ep {
+  k3moe_ep_config c;
+  EpPeerLayout P;
+  EpWsLayout L;
+  char* ws;
+  uint8_t* peer;
+  const uint8_t *w13, *w13_sf, *w2, *w2_sf;
+  EpBases recv_base;  // [d < W]: rank d's region of this rank's rows; [W]: this rank's shared region
+  EpBases back_base;  // [s]: rank s's return buffer
+  EpBases peer_base;  // [s]: rank s's peer buffer
+  bool use_owner;
+};
+
+extern "C" {
+
+size_t k3moe_ep_peer_bytes(const k3moe_ep_config* c) {
+  return ep_config_ok(c) ? (size_t)ep_peer_layout(*c).total : 0;
+}
+
+size_t k3moe_ep_workspace_bytes(const k3moe_ep_config* c) { return ep_config_ok(c) ? ep_ws_layout(*c).total : 0; }
+
+int k3moe_ep_create(const k3moe_ep_config* c, const int32_t* owner, const uint8_t* w13, const uint8_t* w13_sf,
+                    const uint8_t* w2, const uint8_t* w2_sf, void* peer_buffer, const uint64_t* peer_bases,
+                    void* workspace, size_t ws_bytes, k3moe_stream_t stream, k3moe_ep** out) {
+  if (!ep_config_ok(c) || !out || !w13 || !w13_sf || !w2 || !w2_sf || !peer_buffer || !peer_bases || !workspace)
+    return K3MOE_EINVAL;
+  const EpPeerLayout P = ep_peer_layout(*c);
+  const EpWsLayout L = ep_ws_layout(*c);
+  if (ws_bytes < L.total) return K3MOE_ENOSPACE;
+  if (reinterpret_cast<uintptr_t>(peer_buffer) % 256 || reinterpret_cast<uintptr_t>(workspace) % 256 ||
+      peer_bases[c->rank] != reinterpret_cast<uint64_t>(peer_buffer))
+    return K3MOE_EINVAL;
+  for (int s = 0; s < c->world; ++s)
+    if (peer_bases[s] == 0 || peer_bases[s] % 256) return K3MOE_EINVAL;
+  const int El = c->E / c->world;
+  std::vector<int32_t> own(c->E), loc(c->E);
+  if (owner) {
+    std::vector<int> seen(c->world, 0);
+    for (int e = 0; e < c->E; ++e) {
+      if (owner[e] < 0 || owner[e] >= c->world) return K3MOE_EINVAL;
+      own[e] = owner[e];
+      loc[e] = seen[owner[e]]++;
+    }
+    for (int r = 0; r < c->world; ++r)
+      if (seen[r] != El) return K3MOE_EINVAL;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = reinterpret_cast<char*>(workspace);
+  uint8_t* pb = reinterpret_cast<uint8_t*>(peer_buffer);
+  if (cudaMemsetAsync(ws + L.off[EW_EPOCH], 0, 16, s) != cudaSuccess ||
+      cudaMemsetAsync(ws + L.off[EW_ERR], 0, 16, s) != cudaSuccess ||
+      cudaMemsetAsync(pb + P.counts_off, 0, (size_t)(P.total - P.counts_off), s) != cudaSuccess)
+    return K3MOE_ELAUNCH;
+  if (owner && (cudaMemcpyAsync(ws + L.off[EW_OWNER], own.data(), (size_t)c->E * 4, cudaMemcpyHostToDevice, s) !=
+                    cudaSuccess ||
+                cudaMemcpyAsync(ws + L.off[EW_LOCAL], loc.data(), (size_t)c->E * 4, cudaMemcpyHostToDevice, s) !=
+                    cudaSuccess))
+    return K3MOE_ELAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return K3MOE_ELAUNCH;
+  // kernel attributes now, so that a later stream capture needs none
+  if (!set_smem_once(grouped_gemm_kernel<MODE_FC1>, gemm::SMEM_BYTES, 0) ||
+      !set_smem_once(grouped_gemm_kernel<MODE_FC2>, gemm::SMEM_BYTES, 1))
+    return K3MOE_ELAUNCH;
+  const int sc_smem = L.nexp * (TB / 32) * 4;
+  if (sc_smem > 48 * 1024 && !set_smem_once(route_scatter_kernel, sc_smem, 2)) return K3MOE_ELAUNCH;
+  k3moe_ep* ep = new k3moe_ep();
+  ep->c = *c;
+  if (ep->c.wait_budget_ns == 0) ep->c.wait_budget_ns = 5000000000ull;
+  ep->P = P;
+  ep->L = L;
+  ep->ws = ws;
+  ep->peer = pb;
+  ep->w13 = w13;
+  ep->w13_sf = w13_sf;
+  ep->w2 = w2;
+  ep->w2_sf = w2_sf;
+  ep->use_owner = owner != nullptr;
+  for (int d = 0; d < c->world; ++d) {
+    ep->recv_base.base[d] = peer_bases[d] + (uint64_t)P.recv_off + (uint64_t)c->rank * c->max_tokens * P.stride;
+    ep->back_base.base[d] = peer_bases[d] + (uint64_t)P.back_off;
+    ep->peer_base.base[d] = peer_bases[d];
+  }
+  ep->recv_base.base[c->world] = peer_bases[c->rank] + (uint64_t)P.recv_off + (uint64_t)c->world * c->max_tokens * P.stride;
+  *out = ep;
+  return launch_status();
+}
+
+int k3moe_ep_forward_events(k3moe_ep* ep, const float* S, int lds, const float* bias, const void* rs_bf16,
+                            const void* x_bf16, int ldx, int T, void* out_bf16, int ldo, k3moe_stream_t stream,
+                            void* const* events, int n_events) {
+  if (!ep || !S || !bias || !rs_bf16 || !x_bf16 || !out_bf16 || (n_events > 0 && !events)) return K3MOE_EINVAL;
+  const k3moe_ep_config& c = ep->c;
+  const EpPeerLayout& P = ep->P;
+  const EpWsLayout& L = ep->L;
+  if (T < 1 || T > c.max_tokens || lds < c.E || ldx < c.H || ldx % 8 || ldo < c.H || ldo % 8) return K3MOE_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = ep->ws;
+  auto I32 = [&](int i) { return reinterpret_cast<int32_t*>(ws + L.off[i]); };
+  auto U8 = [&](int i) { return reinterpret_cast<uint8_t*>(ws + L.off[i]); };
+  auto mark = [&](int i) {
+    if (i < n_events && events[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(events[i]), s);
+  };
+  const int W = c.world, me = c.rank, K = c.K, H = c.H;
+  u32* err = reinterpret_cast<u32*>(ws + L.off[EW_ERR]);
+  u32* epoch = reinterpret_cast<u32*>(ws + L.off[EW_EPOCH]);
+  u32* counts = reinterpret_cast<u32*>(ep->peer + P.counts_off);
+  const int sms = num_sms(current_device());
+  mark(0);
+  int rc = k3moe_route_topk(S, lds, bias, rs_bf16, T, c.E, K, I32(EW_IDX), reinterpret_cast<float*>(ws + L.off[EW_WTS]),
+                            stream);
+  if (rc) return rc;
+  ep_plan_kernel<<<1, PLAN_THREADS, 0, s>>>(I32(EW_IDX), T, K, W, L.El, ep->use_owner ? I32(EW_OWNER) : nullptr,
+                                            ep->use_owner ? I32(EW_LOCAL) : nullptr, I32(EW_DEST), I32(EW_LID),
+                                            I32(EW_PAIR_POS), I32(EW_PAIR_BACK), I32(EW_SEND_POS), I32(EW_ROWS_TO),
+                                            epoch, counts + W, c.shared ? T : 0, c.E, err);
+  mark(1);
+  {
+    const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
+    const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
+    ep_pack_pairs_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, I32(EW_DEST),
+                                              I32(EW_LID), I32(EW_PAIR_POS), W, 0, nullptr, (int)P.stride, split,
+                                              ep->recv_base, 1, c.shared ? L.El : -1, I32(EW_PAIR_BACK),
+                                              (int)P.back_col);
+  }
+  ep_exchange_kernel<<<1, 32, 0, s>>>(ep->peer_base, P.counts_off, P.flags_off, W, me, 0, I32(EW_ROWS_TO), epoch,
+                                      (unsigned long long)c.wait_budget_ns, err);
+  mark(2);
+  const uint8_t* rows = ep->peer + P.recv_off;
+  {
+    const long long n = (long long)L.R_all * K;
+    const int grid = (int)std::min<long long>(cdiv(n, 256), (long long)sms * 8);
+    ep_ids_k_kernel<<<grid, 256, 0, s>>>(rows, (int)P.stride, L.R_all, H, K, I32(EW_IDS), counts, c.max_tokens);
+  }
+  rc = k3moe_route_tables(I32(EW_IDS), L.R_all, K, 0, L.nexp, 0, 128, ws + L.off[EW_SCRATCH], I32(EW_COUNTS),
+                          I32(EW_CTA_BATCH), I32(EW_CTA_LIMIT), I32(EW_META), I32(EW_ROUTE_MAP), I32(EW_EXP2PERM),
+                          stream);
+  if (rc) return rc;
+  {
+    const int grid = (int)std::min<long long>(cdiv(L.R_all, 8), (long long)sms * 8);
+    ep_unpack_k_kernel<<<grid, 256, 0, s>>>(rows, (int)P.stride, L.R_all, H, K, I32(EW_EXP2PERM), U8(EW_QP),
+                                            U8(EW_SFP));
+  }
+  mark(3);
+  rc = gemm_launch(MODE_FC1, ep->w13, ep->w13_sf, U8(EW_QP), U8(EW_SFP), I32(EW_CTA_BATCH), I32(EW_CTA_LIMIT),
+                   I32(EW_META), U8(EW_FC1Q), U8(EW_FC1SF), nullptr, H, c.I, L.nexp, L.cap_rows, L.max_ctas, err, s,
+                   nullptr, c.activation);
+  if (rc) return rc;
+  mark(4);
+  {
+    const long long n = (long long)L.R_all * K;
+    const int grid = (int)std::min<long long>(cdiv(n, 256), (long long)sms * 8);
+    const unsigned long long shared_rows = reinterpret_cast<unsigned long long>(ws + L.off[EW_SHARED]);
+    ep_step_ptrs_kernel<<<grid, 256, 0, s>>>(I32(EW_EXP2PERM), n, K, rows, (int)P.stride, (int)P.back_col,
+                                             c.max_tokens, W, ep->back_base, (long long)c.max_tokens * K, shared_rows,
+                                             2LL * H, shared_rows + 2ull * H * c.max_tokens,
+                                             reinterpret_cast<unsigned long long*>(ws + L.off[EW_PTRS]), err);
+  }
+  rc = gemm_launch(MODE_FC2, ep->w2, ep->w2_sf, U8(EW_FC1Q), U8(EW_FC1SF), I32(EW_CTA_BATCH), I32(EW_CTA_LIMIT),
+                   I32(EW_META), nullptr, nullptr, nullptr, H, c.I, L.nexp, L.cap_rows, L.max_ctas, err, s, nullptr,
+                   0, 0, 0, 0, 0, reinterpret_cast<const uint64_t*>(ws + L.off[EW_PTRS]));
+  if (rc) return rc;
+  mark(5);
+  ep_exchange_kernel<<<1, 32, 0, s>>>(ep->peer_base, P.counts_off, P.flags_off, W, me, 1, nullptr, epoch,
+                                      (unsigned long long)c.wait_budget_ns, err);
+  mark(6);
+  combine_ep_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const bf16*>(ep->peer + P.back_off), I32(EW_SEND_POS),
+                                      reinterpret_cast<const float*>(ws + L.off[EW_WTS]),
+                                      c.shared ? reinterpret_cast<const bf16*>(ws + L.off[EW_SHARED]) : nullptr, H,
+                                      reinterpret_cast<bf16*>(out_bf16), ldo, T, K, H, H, 0, H, 0);
+  mark(7);
+  return launch_status();
+}
+
+int k3moe_ep_forward(k3moe_ep* ep, const float* S, int lds, const float* bias, const void* rs_bf16,
+                     const void* x_bf16, int ldx, int T, void* out_bf16, int ldo, k3moe_stream_t stream) {
+  return k3moe_ep_forward_events(ep, S, lds, bias, rs_bf16, x_bf16, ldx, T, out_bf16, ldo, stream, nullptr, 0);
+}
+
+uint32_t* k3moe_ep_errors(k3moe_ep* ep) { return ep ? reinterpret_cast<uint32_t*>(ep->ws + ep->L.off[EW_ERR]) : nullptr; }
+
+const uint32_t* k3moe_ep_counts(k3moe_ep* ep) {
+  return ep ? reinterpret_cast<const uint32_t*>(ep->peer + ep->P.counts_off) : nullptr;
+}
+
+const int32_t* k3moe_ep_expert_rows(k3moe_ep* ep) {
+  return ep ? reinterpret_cast<const int32_t*>(ep->ws + ep->L.off[EW_COUNTS]) : nullptr;
+}
+
+const int32_t* k3moe_ep_meta(k3moe_ep* ep) {
+  return ep ? reinterpret_cast<const int32_t*>(ep->ws + ep->L.off[EW_META]) : nullptr;
+}
+
+void k3moe_ep_destroy(k3moe_ep* ep) { delete ep; }
 
 }  // extern "C"
 

@@ -46,11 +46,17 @@ __global__ void __launch_bounds__(256) ep_pairs_kernel(const int* __restrict__ d
 // it goes to, headed by the local ids of its picks there (lid[t*K + k] where dest[t*K + k] == d, in k order);
 // with pair_pos null, slot t headed by `fixed_eid` alone.  Slot p of rank d is row p of dst, or with
 // use_bases, the row at bases.base[d] + p * stride (rank d's receive buffer, possibly in another GPU's memory).
+// With shared_eid >= 0 (use_bases) the token also goes to slot t of bases.base[W], headed by shared_eid alone
+// (the rank's own shared-expert rows).  With pair_back, rank d's row also carries pair_back[t*W + d] (int32) at
+// byte back_col: where the results of the token's picks there go back to.  Stores into peer memory are
+// ordered at system scope before the kernel ends (a later kernel on the stream signals the peers).
 __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restrict__ x, int ldx, int T, int H, int K,
                                                             const int* __restrict__ dest, const int* __restrict__ lid,
                                                             const int* __restrict__ pair_pos, int W, int fixed_eid,
                                                             uint8_t* __restrict__ dst, int stride, int split,
-                                                            EpBases bases, int use_bases) {
+                                                            EpBases bases, int use_bases, int shared_eid = -1,
+                                                            const int* __restrict__ pair_back = nullptr,
+                                                            int back_col = 0) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int pieces = H / 256, share = (pieces + split - 1) / split;
@@ -62,6 +68,8 @@ __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restri
       if (lane == 0) my_pos = t;
     } else if (lane < W) {
       my_pos = pair_pos[(long long)t * W + lane];
+    } else if (lane == W && shared_eid >= 0) {
+      my_pos = t;
     }
     const unsigned live = __ballot_sync(0xffffffffu, my_pos >= 0);
     const bf16* xr = x + (long long)t * ldx;
@@ -89,22 +97,37 @@ __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restri
       int n = 0;
       if (pair_pos == nullptr) {
         ids[n++] = (short)fixed_eid;
+      } else if (lane == W) {
+        ids[n++] = (short)shared_eid;
       } else {
         for (int k = 0; k < K; ++k)
           if (dest[(long long)t * K + k] == lane) ids[n++] = (short)lid[(long long)t * K + k];
+        if (pair_back != nullptr) *reinterpret_cast<int*>(row + back_col) = pair_back[(long long)t * W + lane];
       }
       for (; n < K; ++n) ids[n] = -1;
     }
   }
+  if (use_bases) __threadfence_system();
 }
 
-// ids[i*KH + j] = the j-th local expert id (int16, -1 none) of per-destination row i
+// ids[i*KH + j] = the j-th local expert id (int16, -1 none) of per-destination row i.  With region_counts, the
+// rows come in regions of region_rows rows, region s holding region_counts[s] rows (the rest stale): rows past
+// a region's count get no ids.
 __global__ void __launch_bounds__(256) ep_ids_k_kernel(const uint8_t* __restrict__ rows, int stride, int R, int H,
-                                                       int KH, int* __restrict__ ids) {
+                                                       int KH, int* __restrict__ ids,
+                                                       const u32* __restrict__ region_counts = nullptr,
+                                                       int region_rows = 0) {
   const long long n = (long long)R * KH;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
     const long long i = e / KH;
     const int j = (int)(e - i * KH);
+    if (region_counts != nullptr) {
+      const long long s = i / region_rows;
+      if (i - s * region_rows >= (long long)min(region_counts[s], (u32)region_rows)) {
+        ids[e] = -1;
+        continue;
+      }
+    }
     ids[e] = reinterpret_cast<const short*>(rows + i * stride + H + H / 32)[j];
   }
 }

@@ -9,6 +9,7 @@
 // receiver's wait kernel loads it with acquire semantics before the kernels that read the data start.
 // Every wait is bounded by a %globaltimer budget: on expiry it records ERR_WAIT_TIMEOUT (site 0xA00 + the
 // late source) in the error words and returns; nothing traps.  No TMA touches peer memory.
+#pragma once
 #include "ep.cu"
 
 namespace k3 {

@@ -413,6 +413,9 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
         }
       }
     }
+    // rows stored at caller addresses may sit in a peer GPU's memory: order them at system scope before the
+    // kernel's end (a later kernel on this stream signals the peer)
+    if (MODE == MODE_FC2 && p.out_ptrs != nullptr) __threadfence_system();
     if (p.trace && lane == 0 && warp == 2) {
       atomicAdd(p.trace + MODE * 16 + 5, (unsigned long long)(clock64() - t_role));
       atomicAdd(p.trace + MODE * 16 + 6, (unsigned long long)t_wait);

@@ -77,6 +77,16 @@ SIGNATURES = {
     "k3moe_ipc_import": (_I, [_P, _U64, _P]),
     "k3moe_ipc_release": (_I, [_P, _U64]),
     "k3moe_router_gemm": (_I, [_P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _P]),
+    "k3moe_ep_peer_bytes": (_SZ, [_P]),
+    "k3moe_ep_workspace_bytes": (_SZ, [_P]),
+    "k3moe_ep_create": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P, _P]),
+    "k3moe_ep_forward": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _P, _I, _P]),
+    "k3moe_ep_forward_events": (_I, [_P, _P, _I, _P, _P, _P, _I, _I, _P, _I, _P, _P, _I]),
+    "k3moe_ep_errors": (_P, [_P]),
+    "k3moe_ep_counts": (_P, [_P]),
+    "k3moe_ep_expert_rows": (_P, [_P]),
+    "k3moe_ep_meta": (_P, [_P]),
+    "k3moe_ep_destroy": (None, [_P]),
 }
 
 TRACE_FIELDS = ["producer", "producer_wait_stage", "mma", "mma_wait_loaded", "mma_wait_drained", "epilogue",
@@ -138,6 +148,15 @@ class k3moe_layer_args(ctypes.Structure):
 
 
 ACT_SWIGLU, ACT_SITU = 0, 1
+
+
+class k3moe_ep_config(ctypes.Structure):
+    """include/k3moe.h k3moe_ep_config: one rank's part of the device-resident expert-parallel layer."""
+    _fields_ = [
+        ("world", ctypes.c_int), ("rank", ctypes.c_int), ("H", ctypes.c_int), ("I", ctypes.c_int),
+        ("E", ctypes.c_int), ("K", ctypes.c_int), ("shared", ctypes.c_int), ("max_tokens", ctypes.c_int),
+        ("activation", ctypes.c_int), ("wait_budget_ns", ctypes.c_uint64),
+    ]
 
 
 # ------------------------------------------------------------------ steps

@@ -26,6 +26,9 @@ Per rank (world W, E_local = E / W experts, T local tokens):
 
 The fixed-block mode (decode) sends one row a pick in fixed-size blocks.
 
+DeviceEPMoELayer is the same layer as one C-ABI call a step (k3moe_ep_forward): fixed receive regions in
+peer memory, no host synchronisation, capturable whole in a CUDA graph; the output is the same bytes.
+
 The reference has no MoE all-to-all (its decode EP replicates the batch and
 all-reduces, roofline/decode.md:164-166); this is the token-sharded layout of
 the benchmark configurations.
@@ -603,6 +606,124 @@ def _peer_forward(layer, S, x, events=None):
         events["combine"][1].record()
     shared_rows = layer.shared_out[:T] if layer.shared else None
     return ops.combine(pb.back[:T * K], send_pos, wts, shared_rows, T, K, H)
+
+
+class DeviceEPMoELayer:
+    """One rank's part of the expert-parallel layer as one device-resident C-ABI step (k3moe_ep_forward).
+
+    Every rank allocates one peer buffer (k3moe_ep_peer_bytes) that the others map through CUDA IPC: a fixed
+    region of max_tokens rows a source rank, so no rank needs another's counts before it sends and the step
+    never synchronises with the host; the pack kernel stores rows straight into the destinations' regions and
+    FC2's epilogue stores each result into its owner's return buffer.  w: this rank's weights as for
+    EPMoELayer (slice_weights); owner: as for EPMoELayer (None: contiguous blocks).  With world 1 no process
+    group is needed.  forward() may be captured in a CUDA graph (the same T, buffers and stream)."""
+
+    def __init__(self, H, I, E, K, shared, w, bias, rs, max_tokens, group=None, owner=None, activation=0,
+                 wait_budget_ns=5_000_000_000, device=None):
+        self.group = group
+        distributed = dist.is_available() and dist.is_initialized()
+        self.rank = dist.get_rank(group) if distributed else 0
+        self.world = dist.get_world_size(group) if distributed else 1
+        self.H, self.I, self.E, self.K, self.shared = H, I, E, K, int(shared)
+        self.max_tokens = int(max_tokens)
+        self.w, self.bias, self.rs = w, bias, rs
+        dev = torch.device(device) if device is not None else w["w13"].device
+        cfg = k3moe.k3moe_ep_config(self.world, self.rank, H, I, E, K, self.shared, self.max_tokens, int(activation),
+                                    int(wait_budget_ns))
+        self.cfg = cfg
+        L = k3moe.lib()
+        pbytes = L.k3moe_ep_peer_bytes(ctypes.byref(cfg))
+        wbytes = L.k3moe_ep_workspace_bytes(ctypes.byref(cfg))
+        if pbytes == 0 or wbytes == 0:
+            raise ValueError(f"unsupported expert-parallel configuration {self.world} ranks, E={E}, K={K}, "
+                             f"max_tokens={max_tokens}")
+        self.peer = torch.zeros(pbytes, dtype=torch.uint8, device=dev)
+        self.ws = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+        self._opened = []
+        bases = [0] * self.world
+        bases[self.rank] = self.peer.data_ptr()
+        if self.world > 1:
+            handle = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_uint64()
+            k3moe._check(L.k3moe_ipc_export(self.peer.data_ptr(), ctypes.cast(handle, ctypes.c_void_p),
+                                            ctypes.byref(off)), "ipc_export")
+            torch.cuda.synchronize(dev)
+            every = [None] * self.world
+            dist.all_gather_object(every, (bytes(handle), int(off.value)), group=group)
+            for s, (h, o) in enumerate(every):
+                if s == self.rank:
+                    continue
+                hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                p = ctypes.c_void_p()
+                k3moe._check(L.k3moe_ipc_import(ctypes.cast(hb, ctypes.c_void_p), o, ctypes.byref(p)), "ipc_import")
+                bases[s] = int(p.value)
+                self._opened.append((int(p.value), o))
+        base_arr = (ctypes.c_uint64 * self.world)(*bases)
+        own = None
+        if owner is not None:
+            own = (ctypes.c_int32 * E)(*[int(v) for v in torch.as_tensor(owner).cpu().tolist()])
+        handle = ctypes.c_void_p()
+        k3moe._check(L.k3moe_ep_create(ctypes.byref(cfg), own, k3moe._p(w["w13"]), k3moe._p(w["w13_sf"]),
+                                       k3moe._p(w["w2"]), k3moe._p(w["w2_sf"]), self.peer.data_ptr(),
+                                       ctypes.cast(base_arr, ctypes.c_void_p), self.ws.data_ptr(), wbytes,
+                                       k3moe._stream(), ctypes.byref(handle)), "ep_create")
+        self.handle = handle
+        torch.cuda.synchronize(dev)
+        if self.world > 1:
+            dist.barrier(group=group)  # every rank's flags cleared before any rank's first step
+        self.timing = None
+
+    def forward(self, S, x, out=None, events=None):
+        """out bf16 [T, H] (allocated when None).  events: optional list of up to 8 CUDA events recorded at the
+        step's stage boundaries (k3moe_ep_forward_events)."""
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty((T, self.H), dtype=torch.bfloat16, device=x.device)
+        L = k3moe.lib()
+        if events:
+            for e in events:  # torch creates events lazily: record once so each has a CUDA event
+                e.record()
+            arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+            rc = L.k3moe_ep_forward_events(self.handle, k3moe._p(S), S.stride(0), k3moe._p(self.bias),
+                                           k3moe._p(self.rs), k3moe._p(x), x.stride(0), T, k3moe._p(out),
+                                           out.stride(0), k3moe._stream(), ctypes.cast(arr, ctypes.c_void_p),
+                                           len(events))
+        else:
+            rc = L.k3moe_ep_forward(self.handle, k3moe._p(S), S.stride(0), k3moe._p(self.bias), k3moe._p(self.rs),
+                                    k3moe._p(x), x.stride(0), T, k3moe._p(out), out.stride(0), k3moe._stream())
+        k3moe._check(rc, "ep_forward")
+        return out
+
+    def error_words(self):
+        """The step's two device error words (synchronises; clears them)."""
+        L = k3moe.lib()
+        words = (ctypes.c_uint32 * 2)()
+        rc = L.k3moe_read_error(L.k3moe_ep_errors(self.handle), ctypes.cast(words, ctypes.c_void_p), 1,
+                                k3moe._stream())
+        return rc, (int(words[0]), int(words[1]))
+
+    def received_counts(self):
+        """Rows each source sent this rank in the last step, then this rank's shared rows (host list)."""
+        n = self.world + 1
+        ptr = k3moe.lib().k3moe_ep_counts(self.handle)
+        off = ptr - self.peer.data_ptr()
+        return self.peer[off:off + 4 * n].view(torch.int32).tolist()
+
+    def expert_rows(self):
+        """Rows the last step routed to each local expert (the routed experts, then the shared one): a tensor."""
+        n = self.E // self.world + self.shared
+        off = k3moe.lib().k3moe_ep_expert_rows(self.handle) - self.ws.data_ptr()
+        return self.ws[off:off + 4 * n].view(torch.int32).clone()
+
+    def close(self):
+        """Unmap the peers' buffers and free the host object (after every rank's last step)."""
+        L = k3moe.lib()
+        for p, o in self._opened:
+            L.k3moe_ipc_release(ctypes.c_void_p(p), o)
+        self._opened = []
+        if self.handle:
+            L.k3moe_ep_destroy(self.handle)
+            self.handle = None
 
 
 def slice_weights(w13, w13_sf, w2, w2_sf, E, shared, rank, world, H, I, owner=None):

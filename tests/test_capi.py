@@ -99,3 +99,50 @@ def test_noalloc_limits_match_the_header():
     assert (rows, experts) == (k3moe.NOALLOC_MAX_ROWS, k3moe.NOALLOC_MAX_EXPERTS)
     assert k3moe.lib().k3moe_route_scratch_bytes(rows, experts - 1, 1) == 2 * -(-(rows // 256) * experts * 4 // 256) * 256
     assert k3moe.lib().k3moe_route_scratch_bytes(rows, experts - 1, 1) == 524800
+
+
+def _ep_cfg(**kw):
+    import k3moe
+
+    c = dict(world=8, rank=3, H=7168, I=2048, E=896, K=8, shared=1, max_tokens=8192, activation=0,
+             wait_budget_ns=0)
+    c.update(kw)
+    return k3moe.k3moe_ep_config(**c)
+
+
+def test_ep_step_buffer_sizes(lib):
+    """The device-resident step's peer buffer: (W + 1) regions of max_tokens rows (E4M3 | UE8M0 | int16 ids |
+    int32 return index, 16-byte rows), the return buffer of max_tokens * K bf16 rows, 256 bytes of counts and
+    of flags, each part 256-byte aligned."""
+    c = _ep_cfg()
+    stride = -(-(7168 + 7168 // 32 + 2 * 8 + 4) // 16) * 16
+    assert stride == 7424
+    recv = 9 * 8192 * stride
+    back_off = -(-recv // 256) * 256
+    counts_off = back_off + -(-(8192 * 8 * 7168 * 2) // 256) * 256
+    assert lib.k3moe_ep_peer_bytes(ctypes.byref(c)) == counts_off + 512
+    ws = lib.k3moe_ep_workspace_bytes(ctypes.byref(c))
+    # the GEMM operands dominate: every pick a rank can receive (8 sources x 8192 tokens x 8 picks + the shared
+    # rows), padded to 128 an expert, in MXFP8 (H + H/32) and FC1's output (I + I/32)
+    cap = (112 + 1 + -(-(8 * 8192 * 8 + 8192) // 128)) * 128
+    assert ws > cap * (7168 + 224 + 2048 + 64)
+    assert ws < cap * (7168 + 224 + 2048 + 64 + 8) + 2 ** 28
+
+
+def test_ep_step_rejects_bad_configurations_without_device_work(lib):
+    bad = [dict(world=0), dict(world=17), dict(rank=8), dict(E=900), dict(K=3), dict(K=32), dict(H=1000),
+           dict(I=100), dict(max_tokens=0), dict(activation=2), dict(E=2048, world=8)]
+    for kw in bad:
+        c = _ep_cfg(**kw)
+        assert lib.k3moe_ep_peer_bytes(ctypes.byref(c)) == 0, kw
+        assert lib.k3moe_ep_workspace_bytes(ctypes.byref(c)) == 0, kw
+        out = ctypes.c_void_p()
+        assert lib.k3moe_ep_create(ctypes.byref(c), None, None, None, None, None, None, None, None, 0, None,
+                                   ctypes.byref(out)) == -1, kw
+    assert lib.k3moe_ep_peer_bytes(None) == 0
+    # a valid configuration with missing buffers is refused before any device call
+    out = ctypes.c_void_p()
+    assert lib.k3moe_ep_create(ctypes.byref(_ep_cfg()), None, None, None, None, None, None, None, None, 0, None,
+                               ctypes.byref(out)) == -1
+    assert lib.k3moe_ep_forward(None, None, 896, None, None, None, 7168, 8, None, 7168, None) == -1
+    assert lib.k3moe_ep_errors(None) is None

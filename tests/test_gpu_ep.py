@@ -4,8 +4,11 @@ layer (all experts on one GPU) over all the tokens.  Needs 2 GPUs.  Modes: the
 counts-exchange all-to-all, the fixed-block all-to-all, the fixed-block step
 captured in a CUDA graph (NCCL calls inside) and replayed, experts dealt to
 the ranks by router bias instead of contiguous blocks, FC2 in column slices
-returned beside the next slice, and the peer-memory transport (rows and
-results stored into the peers' buffers over NVLink, flags, bounded waits)."""
+returned beside the next slice, the peer-memory transport (rows and
+results stored into the peers' buffers over NVLink, flags, bounded waits),
+and the device-resident step (k3moe_ep_forward: fixed receive regions, no host
+synchronisation) eagerly, with experts placed by bias, and captured whole in a
+CUDA graph."""
 import multiprocessing as mp
 import os
 import socket
@@ -60,17 +63,21 @@ def _worker(rank, world, port, outdir, mode):
     bias = torch.from_numpy(rng.uniform(-0.1, 0.1, E).astype(np.float32)).to(dev)
     rs = torch.tensor([c["rs"]], dtype=torch.bfloat16, device=dev)
     rows = slice(rank * c["T_local"], (rank + 1) * c["T_local"])
-    owner = k3moe_ep.balanced_owner(bias, world) if mode == "placed" else None
+    owner = k3moe_ep.balanced_owner(bias, world) if mode in ("placed", "device_placed") else None
     w = k3moe_ep.slice_weights(w13, w13_sf, w2, w2_sf, E, sh, rank, world, H, I, owner=owner)
-    layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev,
-                                fixed_tokens=c["T_local"] if mode in ("fixed", "graph") else None, owner=owner,
-                                overlap_chunks=2 if mode == "overlap" else 1,
-                                fc2_grid_cap=100 if mode == "overlap" else 0,
-                                transport="peer" if mode == "peer" else "nccl",
-                                max_tokens=c["T_local"] if mode == "peer" else None)
+    if mode.startswith("device"):
+        layer = k3moe_ep.DeviceEPMoELayer(H, I, E, K, sh, w, bias, rs, max_tokens=c["T_local"], owner=owner,
+                                          device=dev)
+    else:
+        layer = k3moe_ep.EPMoELayer(H, I, E, K, sh, w, bias, rs, device=dev,
+                                    fixed_tokens=c["T_local"] if mode in ("fixed", "graph") else None, owner=owner,
+                                    overlap_chunks=2 if mode == "overlap" else 1,
+                                    fc2_grid_cap=100 if mode == "overlap" else 0,
+                                    transport="peer" if mode == "peer" else "nccl",
+                                    max_tokens=c["T_local"] if mode == "peer" else None)
     xs, Ss = x[rows].contiguous(), S[rows].contiguous()
     graph = None
-    if mode == "graph":
+    if mode in ("graph", "device_graph"):
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -101,8 +108,9 @@ def _worker(rank, world, port, outdir, mode):
         ok = ok and not bad_rows
         open(os.path.join(outdir, "result"), "w").write(
             "ok" if ok else f"mismatch: repeat-equal={ok} rows={bad_rows[:20]} n={len(bad_rows)} maxdiff={diff}")
-    if mode == "peer":  # the waits recorded nothing, and the peers' buffers are unmapped before the group goes
-        words = layer.ops.err[:2].tolist()
+    if mode == "peer" or mode.startswith("device"):
+        # the waits recorded nothing, and the peers' buffers are unmapped before the group goes
+        words = layer.ops.err[:2].tolist() if mode == "peer" else list(layer.error_words()[1])
         if rank == 0 and words != [0, 0]:
             open(os.path.join(outdir, "result"), "w").write(f"device error words {words}")
         dist.barrier()
@@ -115,7 +123,8 @@ def _worker(rank, world, port, outdir, mode):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed", "overlap", "peer"])
+@pytest.mark.parametrize("mode", ["counts", "fixed", "graph", "placed", "overlap", "peer", "device",
+                                  "device_placed", "device_graph"])
 def test_ep2_nccl_bit_identical_to_one_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
