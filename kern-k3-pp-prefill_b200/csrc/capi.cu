@@ -763,7 +763,7 @@ struct EpPeerLayout {
 
 EpPeerLayout ep_peer_layout(const k3moe_ep_config& c) {
   EpPeerLayout L;
-  L.back_col = (long long)c.H + c.H / 32 + 2LL * c.K;
+  L.back_col = ((long long)c.H + c.H / 32 + 2LL * c.K + 3) / 4 * 4;  // the int32 after the ids, 4-byte aligned
   L.stride = (L.back_col + 4 + 15) / 16 * 16;
   L.recv_off = 0;
   L.back_off = (long long)align_up((size_t)(c.world + 1) * c.max_tokens * L.stride, 256);

@@ -121,6 +121,10 @@ def test_ep_step_buffer_sizes(lib):
     back_off = -(-recv // 256) * 256
     counts_off = back_off + -(-(8192 * 8 * 7168 * 2) // 256) * 256
     assert lib.k3moe_ep_peer_bytes(ctypes.byref(c)) == counts_off + 512
+    # K = 1: the return index after one int16 id is moved to the next 4-byte boundary (7392 + 2 -> 7396)
+    c1 = _ep_cfg(K=1, world=2, rank=0, E=16, max_tokens=64)
+    recv1 = 3 * 64 * -(-(7396 + 4) // 16) * 16
+    assert lib.k3moe_ep_peer_bytes(ctypes.byref(c1)) == -(-recv1 // 256) * 256 + 64 * 7168 * 2 + 512
     ws = lib.k3moe_ep_workspace_bytes(ctypes.byref(c))
     # the GEMM operands dominate: every pick a rank can receive (8 sources x 8192 tokens x 8 picks + the shared
     # rows), padded to 128 an expert, in MXFP8 (H + H/32) and FC1's output (I + I/32)
