@@ -331,7 +331,8 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
       const Unit w = decode_unit(p, u);
       if (!w.valid) continue;
       const long long t0 = clock64();
-      if (!mbar_wait(acc_full, acc_phase, abort_flag, p.err, 0x700u + MODE)) break;
+      // the warp leaves together (its tensor-memory loads and shuffles below take every lane)
+      if (!__all_sync(0xffffffffu, mbar_wait(acc_full, acc_phase, abort_flag, p.err, 0x700u + MODE))) break;
       t_wait += clock64() - t0;
       tc_fence_after();
       u32 v[4][32];
@@ -353,9 +354,58 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       acc_phase ^= 1u;
-      if (row < w.n) {
+      if (MODE == MODE_FC2) {
+        // The thread's 128 columns of its token row, as bf16.  Stored one row a lane, a warp's store would
+        // touch 32 lines (32 L1 wavefronts for 1 KB); instead each group of 8 lanes transposes its 8 rows'
+        // 16-byte chunks (lane i gets chunk i of each row) and stores whole 128-byte lines: 4 lines a store.
+        bf16* dst = nullptr;
+        if (row < w.n) {
+          const long long r = w.row0 + row;
+          if (p.out_ptrs != nullptr) {
+            dst = reinterpret_cast<bf16*>(p.out_ptrs[r]) + (p.fb0 + w.fb) * BN + 128 * half;
+          } else {
+            const long long ro = p.out_rows ? (long long)p.out_rows[r] : r;
+            dst = p.out_bf16 + ro * p.out_cols + w.fb * BN + 128 * half;
+          }
+        }
+        const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {  // 64 columns at a time: 8 chunks of 16 bytes
+          uint4 a[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const u32* src = v[2 * g + c / 4] + 8 * (c % 4);
+            a[c] = make_uint4(f2_to_bf16x2(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                              f2_to_bf16x2(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                              f2_to_bf16x2(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                              f2_to_bf16x2(__uint_as_float(src[6]), __uint_as_float(src[7])));
+          }
+          // 8 x 8 transpose within each 8-lane group: swap off-diagonal blocks of 4, then 2, then 1
+#pragma unroll
+          for (int d = 4; d >= 1; d >>= 1) {
+            const bool upper = (lane & d) != 0;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              if (c & d) continue;
+              const uint4 send = upper ? a[c] : a[c | d];
+              uint4 got;
+              got.x = __shfl_xor_sync(0xffffffffu, send.x, d);
+              got.y = __shfl_xor_sync(0xffffffffu, send.y, d);
+              got.z = __shfl_xor_sync(0xffffffffu, send.z, d);
+              got.w = __shfl_xor_sync(0xffffffffu, send.w, d);
+              if (upper) a[c] = got;
+              else a[c | d] = got;
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {  // row (group base + m), chunk (lane % 8)
+            const unsigned long long rp = __shfl_sync(0xffffffffu, mine, (lane & ~7) | m);
+            if (rp != 0ull) *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(rp) + 64 * g + 8 * (lane & 7)) = a[m];
+          }
+        }
+      } else if (row < w.n) {
         const long long r = w.row0 + row;
-        if (MODE == MODE_FC1) {
+        {
           const int kg4 = p.out_cols / 128;
           // SiTU's a, b: per expert from the caller's buffers (the module entry), else K3's 4 and 25
           float ga = 4.0f, gra = 0.25f, gb = 25.0f, grb = 0.04f;
@@ -391,25 +441,6 @@ __device__ __forceinline__ void grouped_gemm_body(const CUtensorMap* tmW, const 
           // the two groups' scales are adjacent bytes of one atom row (kb even)
           const int kb = (w.fb * 128 + 64 * half) / 32;
           *reinterpret_cast<unsigned short*>(p.out_sf + sf_tiled_offset(r, kb, kg4)) = (unsigned short)sfw;
-        } else {
-          bf16* dst;
-          if (p.out_ptrs != nullptr) {
-            dst = reinterpret_cast<bf16*>(p.out_ptrs[r]) + (p.fb0 + w.fb) * BN + 128 * half;
-          } else {
-            const long long ro = p.out_rows ? (long long)p.out_rows[r] : r;
-            dst = p.out_bf16 + ro * p.out_cols + w.fb * BN + 128 * half;
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 16) {  // 16 columns, 32 bytes a store
-              u32 o[8];
-#pragma unroll
-              for (int h = 0; h < 8; ++h)
-                o[h] = f2_to_bf16x2(__uint_as_float(v[q][j + 2 * h]), __uint_as_float(v[q][j + 2 * h + 1]));
-              st_global_v8(dst + 32 * q + j, o);
-            }
-          }
         }
       }
     }
