@@ -135,6 +135,44 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ inputs (both arms)
+def gpu_local_cpus(dev):
+    """The host CPUs NVML reports as local to `dev` (its NUMA node), or None when NVML cannot say."""
+    try:
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+        words = (os.cpu_count() + 63) // 64
+        masks = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {64 * i + b for i, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
+
+
+class LocalHost:
+    """Runs the block with this process on the host CPUs local to `dev`: pinned buffers allocated inside are
+    first touched there, so they sit in the GPU's own NUMA node and N ranks' host copies spread over the
+    sockets' memory instead of all crossing into one node.  The previous affinity comes back on exit."""
+
+    def __init__(self, dev):
+        self.dev, self.prev = dev, None
+
+    def __enter__(self):
+        cpus = gpu_local_cpus(self.dev)
+        if cpus:
+            self.prev = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, cpus)
+        self.cpus = len(cpus) if cpus else None
+        return self
+
+    def __exit__(self, *a):
+        if self.prev:
+            os.sched_setaffinity(0, self.prev)
+
+
 def bf16_round(a):
     """f32 -> bf16 bit patterns, round to nearest even (numpy)."""
     u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
@@ -594,11 +632,12 @@ def run_ep(args, world, rank, dev):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, disp_ms, comb_ms, fc1_ms = [float(v) for v in t.tolist()]
     # e2e: x and S from pinned host memory in, the output back, every step (copies overlapped)
-    x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
-    dist.barrier()
-    n_e2e = args.e2e_steps or args.steps
-    e2e_ms = e2e_overlapped(lambda Sd, xd, od: layer.forward(Sd, xd), S_h, x_h, (T, H), n_e2e,
-                            torch.cuda.current_stream(), dev)
+    with LocalHost(dev) as local:
+        x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
+        dist.barrier()
+        n_e2e = args.e2e_steps or args.steps
+        e2e_ms = e2e_overlapped(lambda Sd, xd, od: layer.forward(Sd, xd), S_h, x_h, (T, H), n_e2e,
+                                torch.cuda.current_stream(), dev)
     t = torch.tensor([e2e_ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
@@ -644,7 +683,8 @@ def run_ep(args, world, rank, dev):
                     "h2d_bytes_per_step": int(x.numel() * 2 + S.numel() * 4) * world,
                     "d2h_bytes_per_step": int(x.numel() * 2) * world,
                     "copies": "every step's x, S in and output back over PCIe, on side streams overlapping the "
-                              "neighbouring steps' compute (double buffers)"},
+                              "neighbouring steps' compute (double buffers)",
+                    "host_buffers": "pinned on each GPU's local NUMA node" if local.cpus else "NUMA placement unknown"},
             # nccl / peer: topk, 2 x 3 plan launches, pairs, pack, shared pack, ids, 3 table launches, unpack,
             # return rows, FC1, FC2 (a launch a slice), combine (+ peer: row pointers, 2 signals, 2 waits);
             # device: topk, plan, pack, exchange, ids, 3 table launches, unpack, FC1, row pointers, FC2,
@@ -821,6 +861,7 @@ def run_decode(args, world, rank, dev):
     with ClockSampler(uuid) as clk:
         us = timed(graph.replay)
     # end to end: this rank's x and S from pinned host memory into the step's inputs, its output back
+    local = LocalHost(dev).__enter__()  # pinned buffers on this GPU's NUMA node (restored below)
     x_h, S_h = x.cpu().pin_memory(), S.cpu().pin_memory()
     out_h = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
     if world > 1:
@@ -836,6 +877,7 @@ def run_decode(args, world, rank, dev):
     e1.record()
     torch.cuda.synchronize()
     e2e_us = max_over_ranks(e0.elapsed_time(e1) / n_e2e * 1e3)
+    local.__exit__()
     # bytes a layer must stream on the slowest rank: its touched experts' weights (+ the shared expert's)
     if world == 1:
         off = layer.offsets(T)
@@ -1199,14 +1241,15 @@ def main():
 
     # ---------------- end to end through the public API: host x/S in, host out back
     e2e_steps = args.e2e_steps or args.steps
-    x_h = x.cpu().pin_memory()
-    S_h = S.cpu().pin_memory()
 
     def fwd(Sd, xd, od):
         layer.forward(Sd, xd, od)
         return od
 
-    e2e_ms = e2e_overlapped(fwd, S_h, x_h, (T, H), e2e_steps, stream, dev)
+    with LocalHost(dev):
+        x_h = x.cpu().pin_memory()
+        S_h = S.cpu().pin_memory()
+        e2e_ms = e2e_overlapped(fwd, S_h, x_h, (T, H), e2e_steps, stream, dev)
     layer.check_device_error(T)
 
     # ---------------- the router GEMM (the step before the path, outside the layer's time): this build's
