@@ -681,7 +681,7 @@ static_assert(F_MAX_ROWS <= 64, "an expert's picking rows fit a 64-bit mask");
 static_assert(F_SORT_WARPS % 4 == 0, "warp maxima read four at a time");
 
 // Up to this many rows every shared-expert block computes the SiTU rows itself instead of waiting for the row
-// blocks' flags (and stages its weight rows with one bulk copy)
+// blocks' flags
 constexpr int F_LOCAL_SITU_ROWS = 8;
 static_assert(F_LOCAL_SITU_ROWS * (F_SH / 8) <= F_WORKERS, "one act chunk a thread");
 static_assert(F_RANK_WARPS >= 2 && F_SORT_WARPS <= 31 && F_SORT_WARPS >= TOPK,
@@ -889,7 +889,6 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
   __shared__ int s_last, s_fail;
   __shared__ u32 s_tmem;
   __shared__ __align__(8) u64 s_bar;
-  __shared__ __align__(8) u64 s_wbar;
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;");
   const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -1069,48 +1068,25 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
     tmem_alloc(&s_tmem, 64);
     tmem_relinquish();
   }
-  // Wsh's 64 rows (one contiguous 96 KB run).  With the act rows coming from the row blocks, the act region is
-  // needed for them: the rows go straight into the swizzled operand, 16 bytes a cp.async, in flight with the
-  // act rows' copies.  With few rows, one bulk copy (the TMA unit) stages them in the act region and the block
-  // swizzles them in shared memory, which lands them sooner.
-  if (!local_act)
-    for (int i = t; i < 64 * (F_SH / 8); i += F_WORKERS) {
-      const int r = i / (F_SH / 8), k = i % (F_SH / 8);
-      cp_async16(sw_at + front_swizzle(r, k), wsh + (long long)(n0 + r) * F_SH + k * 8);
-    }
+  // Wsh's 64 rows (one contiguous 96 KB run) go straight into the swizzled operand, 16 bytes a cp.async, in
+  // flight with the act rows' loads.  (Staging them with one bulk copy and swizzling them in shared memory was
+  // 0.6 us slower a launch at 8 rows.)
+  for (int i = t; i < 64 * (F_SH / 8); i += F_WORKERS) {
+    const int r = i / (F_SH / 8), k = i % (F_SH / 8);
+    cp_async16(sw_at + front_swizzle(r, k), wsh + (long long)(n0 + r) * F_SH + k * 8);
+  }
   if (t == 0) {
     s_fail = 0;
-    mbar_init(&s_wbar, 1);
     mbar_init(&s_bar, 1);
     fence_mbar_init();
-    if (local_act) {
-      mbar_arrive_expect_tx(&s_wbar, (u32)F_OPERAND);
-      bulk_load(sa, wsh + (long long)n0 * F_SH, (u32)F_OPERAND, &s_wbar);
-    }
   }
   front_work_sync();
   if (local_act) {
-    if (mbar_wait(&s_wbar, 0, nullptr, nullptr, 0, F_WAIT_NS)) {
-      // the staged rows into the swizzled K-major operand, 16 bytes a step (conflict-free both ways)
-      constexpr int CHUNKS = 64 * (F_SH / 8), PER = (CHUNKS + F_WORKERS - 1) / F_WORKERS;
-      uint4 v[PER];
-#pragma unroll
-      for (int m = 0; m < PER; ++m)
-        if (t + m * F_WORKERS < CHUNKS) v[m] = reinterpret_cast<const uint4*>(sa)[t + m * F_WORKERS];
-#pragma unroll
-      for (int m = 0; m < PER; ++m) {
-        const int i = t + m * F_WORKERS;
-        if (i < CHUNKS) *reinterpret_cast<uint4*>(sw + front_swizzle(i / (F_SH / 8), i % (F_SH / 8))) = v[m];
-      }
-    } else {
-      s_fail = 1;
-      atomicOr(done, F_ERR);
-    }
-    front_work_sync();  // the staging area read out: the act rows may land there
     if (my_chunk)
       *reinterpret_cast<uint4*>(sa + front_swizzle(ar, ak)) =
           make_uint4(situ_bf16x2(g0.x, g0.y, u0.x, u0.y), situ_bf16x2(g0.z, g0.w, u0.z, u0.w),
                      situ_bf16x2(g1.x, g1.y, u1.x, u1.y), situ_bf16x2(g1.z, g1.w, u1.z, u1.w));
+    cp_async_wait_all();
   } else {
     if (t < T) {
       int* flag = ready + c * 64 + t;
