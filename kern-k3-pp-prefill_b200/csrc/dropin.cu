@@ -505,7 +505,10 @@ extern "C" __global__ void __launch_bounds__(1024) kern_k3g_moe_route_init(u32* 
 
 // K3's shared-expert SiTU on landed bf16 operands (kern_k3g_situ, source/k3_prefill_glue.cu:668-686): p = [gate |
 // up] rows of 2n bf16, act [B, n] bf16.  Grid (B, ceil(n / 2048)), block 256, 8 columns a thread (n a
-// multiple of 8); the fused front's arithmetic (situ_front).
+// multiple of 8); the fused front's arithmetic (situ_front).  The reference entry switches a warp to an
+// approximate reciprocal with one Newton step when every gate is >= -87; the reference records that step equal
+// to the correctly rounded reciprocal for every d in [2^-126, 2^126) (source/k3_moe_route.cu:78-80, checked
+// over all of them), which holds 1 + e^-g there, so __frcp_rn on every lane gives the same bytes.
 extern "C" __global__ void __launch_bounds__(256) kern_k3g_situ(const bf16* __restrict__ p, bf16* __restrict__ act,
                                                                  int n, int B) {
   const int b = blockIdx.x;
