@@ -618,7 +618,7 @@ def run_ep(args, world, rank, dev):
     with ClockSampler(uuid) as clk:
         start.record()
         for s in range(args.steps):
-            layer.forward(S, x, evs[s])
+            layer.forward(S, x, events=evs[s])
         stop.record()
         torch.cuda.synchronize()
     dist.barrier()
