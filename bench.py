@@ -580,7 +580,8 @@ def full_layer(E, bias, rs, T, dev):
 # ------------------------------------------------------------------ the GPU arm, N > 1: expert parallel
 def run_ep(args, world, rank, dev):
     """Config 4's layout at N GPUs: every rank owns an 8192-row chunk (16 packed sequences) and E/N experts
-    (+ the shared expert); dispatch and combine are NCCL all-to-all; weak scaling (N x 8192 rows a step).
+    (+ the shared expert); dispatch and combine by the chosen transport (default: the device-resident step, one
+    C-ABI call with peer-memory stores and no host synchronisation); weak scaling (N x 8192 rows a step).
     After timing, every rank checks its output against the 1-GPU layer over all experts on its own rows
     (`ep_bit_identical`, all ranks), and a config-2 decode step (64 tokens over the N ranks) is timed as a
     CUDA graph and checked the same way (`decode`)."""
@@ -708,7 +709,8 @@ DECODE_METRIC = "EP decode us/layer (64 tokens x top-8)"
 
 def decode_pass(args, world, rank, dev, w, owner, full):
     """Config 2 inside the expert-parallel run: 64 tokens (rank r owns rows [r T, r T + T) of one global batch)
-    through this rank's experts `w`, fixed-size all-to-all blocks (no host synchronisation), the whole step
+    through this rank's experts `w` by the device-resident step (transport "device"), or with fixed-size
+    all-to-all blocks over NCCL (the other transports); neither synchronises with the host, and the whole step is
     captured as one CUDA graph and replayed.  Returns us a layer (max over ranks), an eager breakdown, and
     whether every rank's output equals the 1-GPU layer `full` on the same rows."""
     import torch
@@ -1128,7 +1130,7 @@ def main():
                     help="N > 1 with --ep-overlap > 1: FC2's persistent blocks (0: one an SM), SMs left to NCCL")
     ap.add_argument("--no-reference-kernels", action="store_true",
                     help="skip the leg that times the reference's GEMM family (FlashInfer TRT-LLM-gen) on this GPU")
-    ap.add_argument("--ep-transport", default="nccl", choices=["nccl", "peer", "device"],
+    ap.add_argument("--ep-transport", default="device", choices=["nccl", "peer", "device"],
                     help="N > 1: the two all-to-alls over NCCL; stores into the peers' buffers over NVLink after "
                          "a counts exchange (peer); or the device-resident step, one C-ABI call with fixed peer "
                          "regions and no host synchronisation (device)")
