@@ -587,9 +587,10 @@ int k3moe_ep_pack_pairs(const void* x_bf16, int ldx, int T, int H, int K, const 
   const int sms = num_sms(current_device());
   const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
   const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
-  ep_pack_pairs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  const int tail = split == 1 ? stride - H : 0;  // one warp a token: row tails built in shared memory
+  ep_pack_pairs_kernel<<<grid, 256, 8 * tail, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, fixed_eid, dst, stride, split,
-      EpBases{}, 0);
+      EpBases{}, 0, -1, nullptr, 0, tail);
   return launch_status();
 }
 
@@ -608,8 +609,10 @@ int k3moe_ep_pack_pairs_to(const void* x_bf16, int ldx, int T, int H, int K, con
   const int sms = num_sms(current_device());
   const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
   const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
-  ep_pack_pairs_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, 0, nullptr, stride, split, b, 1);
+  const int tail = split == 1 ? stride - H : 0;  // one warp a token: row tails built in shared memory
+  ep_pack_pairs_kernel<<<grid, 256, 8 * tail, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, dest, lid, pair_pos, W, 0, nullptr, stride, split, b, 1,
+      -1, nullptr, 0, tail);
   return launch_status();
 }
 
@@ -959,10 +962,11 @@ int k3moe_ep_forward_events(k3moe_ep* ep, const float* S, int lds, const float* 
   {
     const int split = (int)std::max<long long>(1, std::min<long long>(H / 256, cdiv(4LL * sms, T)));
     const int grid = (int)std::min<long long>(cdiv((long long)T * split, 8), (long long)sms * 8);
-    ep_pack_pairs_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K, I32(EW_DEST),
-                                              I32(EW_LID), I32(EW_PAIR_POS), W, 0, nullptr, (int)P.stride, split,
-                                              ep->recv_base, 1, c.shared ? L.El : -1, I32(EW_PAIR_BACK),
-                                              (int)P.back_col);
+    const int tail = split == 1 ? (int)P.stride - H : 0;  // one warp a token: row tails in shared memory
+    ep_pack_pairs_kernel<<<grid, 256, 8 * tail, s>>>(reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K,
+                                                     I32(EW_DEST), I32(EW_LID), I32(EW_PAIR_POS), W, 0, nullptr,
+                                                     (int)P.stride, split, ep->recv_base, 1, c.shared ? L.El : -1,
+                                                     I32(EW_PAIR_BACK), (int)P.back_col, tail);
   }
   ep_exchange_kernel<<<1, 32, 0, s>>>(ep->peer_base, P.counts_off, P.flags_off, W, me, 0, I32(EW_ROWS_TO), epoch,
                                       (unsigned long long)c.wait_budget_ns, err);

@@ -50,16 +50,23 @@ __global__ void __launch_bounds__(256) ep_pairs_kernel(const int* __restrict__ d
 // (the rank's own shared-expert rows).  With pair_back, rank d's row also carries pair_back[t*W + d] (int32) at
 // byte back_col: where the results of the token's picks there go back to.  Stores into peer memory are
 // ordered at system scope before the kernel ends (a later kernel on the stream signals the peers).
+// With tail_bytes > 0 (= stride - H, a multiple of 16) and split 1, each warp builds a row's tail (scales, ids,
+// return index, zero padding) in tail_bytes of dynamic shared memory and stores it as 16-byte chunks, whole
+// 128-byte lines where the rows are line-aligned, instead of one 4-byte store a scale word and one 2-byte
+// store an id: a row bound for another GPU crosses NVLink as full lines only.
 __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restrict__ x, int ldx, int T, int H, int K,
                                                             const int* __restrict__ dest, const int* __restrict__ lid,
                                                             const int* __restrict__ pair_pos, int W, int fixed_eid,
                                                             uint8_t* __restrict__ dst, int stride, int split,
                                                             EpBases bases, int use_bases, int shared_eid = -1,
                                                             const int* __restrict__ pair_back = nullptr,
-                                                            int back_col = 0) {
+                                                            int back_col = 0, int tail_bytes = 0) {
+  extern __shared__ __align__(16) uint8_t pack_tails[];
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int pieces = H / 256, share = (pieces + split - 1) / split;
+  const bool whole_tail = tail_bytes > 0 && split == 1;
+  uint8_t* tail = pack_tails + (threadIdx.x >> 5) * tail_bytes;
   for (int g = blockIdx.x * warps + (threadIdx.x >> 5); g < T * split; g += gridDim.x * warps) {
     const int t = g / split, part = g - t * split;
     // lane d < W: rank d's slot for this token (or -1)
@@ -88,8 +95,39 @@ __global__ void __launch_bounds__(256) ep_pack_pairs_kernel(const bf16* __restri
         const long long pd = __shfl_sync(0xffffffffu, my_pos, d);
         uint8_t* row = (use_bases ? reinterpret_cast<uint8_t*>(bases.base[d]) : dst) + pd * stride;
         *reinterpret_cast<uint2*>(row + c) = w;
-        if ((lane & 15) == 0) *reinterpret_cast<u32*>(row + H + kb) = sfw;
+        if (!whole_tail && (lane & 15) == 0) *reinterpret_cast<u32*>(row + H + kb) = sfw;
       }
+      if (whole_tail && (lane & 15) == 0) *reinterpret_cast<u32*>(tail + kb) = sfw;
+    }
+    if (whole_tail) {
+      // per destination: its ids and return index into the tail image, then the tail out in 16-byte chunks
+      for (unsigned m = live; m; m &= m - 1) {
+        const int d = __ffs(m) - 1;
+        __syncwarp();
+        if (lane == d) {
+          short* ids = reinterpret_cast<short*>(tail + H / 32);
+          int n = 0;
+          if (pair_pos == nullptr) {
+            ids[n++] = (short)fixed_eid;
+          } else if (lane == W) {
+            ids[n++] = (short)shared_eid;
+          } else {
+            for (int k = 0; k < K; ++k)
+              if (dest[(long long)t * K + k] == lane) ids[n++] = (short)lid[(long long)t * K + k];
+          }
+          for (; n < K; ++n) ids[n] = -1;
+          for (int b = H / 32 + 2 * K; b < tail_bytes; b += 2) *reinterpret_cast<short*>(tail + b) = 0;
+          if (pair_back != nullptr && lane < W)
+            *reinterpret_cast<int*>(tail + (back_col - H)) = pair_back[(long long)t * W + lane];
+        }
+        __syncwarp();
+        const long long pd = __shfl_sync(0xffffffffu, my_pos, d);
+        uint8_t* row = (use_bases ? reinterpret_cast<uint8_t*>(bases.base[d]) : dst) + pd * stride;
+        for (int q = lane; q < tail_bytes / 16; q += 32)
+          *reinterpret_cast<uint4*>(row + H + 16 * q) = reinterpret_cast<const uint4*>(tail)[q];
+      }
+      __syncwarp();
+      continue;
     }
     if (part == 0 && my_pos >= 0) {  // lane d writes its rank's id list
       uint8_t* row = (use_bases ? reinterpret_cast<uint8_t*>(bases.base[lane]) : dst) + my_pos * stride;
