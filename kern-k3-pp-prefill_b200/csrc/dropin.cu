@@ -664,6 +664,8 @@ namespace dropin {
 constexpr int F_EXPERTS = K3F_EXPERTS, F_LDS = K3F_LDS, F_SH = K3F_SH, F_STRIDE = K3F_STRIDE, F_NSH = K3F_NSH;
 constexpr int F_LOCAL = F_EXPERTS / F_STRIDE;  // this rank's experts
 constexpr int F_TILE = 16, F_MAX_ROWS = 64;
+// CTAs of the tables: ceil(rows / F_TILE) an expert, at most one partial CTA a local expert
+constexpr int F_MAX_CTAS = F_LOCAL + F_MAX_ROWS * TOPK / F_TILE;
 constexpr int F_READERS = F_NSH / 64;           // shared-expert blocks
 constexpr int F_THREADS = 1024, F_WORKERS = F_THREADS - 32;
 constexpr int F_SORT_WARPS = F_EXPERTS / 32;    // an expert a thread
@@ -774,14 +776,18 @@ __device__ __forceinline__ void front_work_sync() {
 __device__ __forceinline__ void front_tables(const int* __restrict__ idx, int first, int T, u64* __restrict__ scratch,
                                              int* __restrict__ cta_batch, int* __restrict__ cta_limit,
                                              int* __restrict__ num_non_exiting, int* __restrict__ total_padded,
-                                             int* __restrict__ route_map, int* __restrict__ exp2perm) {
+                                             int* __restrict__ route_map, int* __restrict__ exp2perm, int own_row,
+                                             const int* __restrict__ own_picks) {
   using namespace dropin;
   u64* rows = scratch;                                   // [F_LOCAL] the rows picking each expert
   int* off = reinterpret_cast<int*>(rows + F_LOCAL);     // [F_LOCAL + 1] first CTA of each expert
+  int* clim = off + F_LOCAL + 1;                         // [F_MAX_CTAS] end of each CTA's real rows
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31, r = t / TOPK;
   int j = -1;
   if (t < T * TOPK) {
-    const int d = __ldcg(idx + t) - first;
+    // this block's own row from shared memory; the others' from L2, where their blocks stored them before
+    // counting in
+    const int d = (r == own_row ? own_picks[t - r * TOPK] : __ldcg(idx + t)) - first;
     if (d >= 0 && d % F_STRIDE == 0 && d / F_STRIDE < F_LOCAL) j = d / F_STRIDE;
   }
   if (j >= 0) atomicOr(rows + j, 1ull << r);  // rows[] zeroed by the caller before its last barrier
@@ -818,10 +824,11 @@ __device__ __forceinline__ void front_tables(const int* __restrict__ idx, int fi
   if (t < F_LOCAL) {
     const int o0 = off[t], o1 = off[t + 1], lim = o0 * F_TILE + __popcll(rows[t]);
     for (int c = o0; c < o1; ++c) {
+      const int l = min((c + 1) * F_TILE, lim);
       cta_batch[c] = t;
-      cta_limit[c] = min((c + 1) * F_TILE, lim);
+      cta_limit[c] = l;
+      clim[c] = l;
     }
-    for (int p = lim; p < o1 * F_TILE; ++p) route_map[p] = 0;
   }
   if (t < T * TOPK) {
     int row = -1;
@@ -831,6 +838,10 @@ __device__ __forceinline__ void front_tables(const int* __restrict__ idx, int fi
     }
     exp2perm[t] = row;
   }
+  __syncthreads();
+  // the padding rows (route token 0), one a thread over all CTAs' slots
+  for (int i = t; i < off[F_LOCAL] * F_TILE; i += blockDim.x)
+    if (i >= clim[i / F_TILE]) route_map[i] = 0;
 }
 
 // Warp 31 of shared-expert block c: the rows' lowest local picks (clearing their flags), then this block's
@@ -1038,7 +1049,7 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
     __syncthreads();
     if (!s_last) return;
     front_tables(idx, first, T, table_scratch, cta_batch, cta_limit, num_non_exiting, total_padded,
-                 route_map, exp2perm);
+                 route_map, exp2perm, b, s_pick);
     __syncthreads();
     if (t == 0) atomicAnd(done, F_ERR);  // the count back to zero, a recorded error kept
     return;
