@@ -687,8 +687,11 @@ static_assert(F_SORT_WARPS % 4 == 0, "warp maxima read four at a time");
 
 // Up to this many rows every shared-expert block computes the SiTU rows itself instead of waiting for the row
 // blocks' flags
+// (16 rows, two chunks a thread, was slower from 8 rows up: 7.66 -> 8.55 us at 16 rows, the extra S reads
+// costing more than the flag wait they save)
 constexpr int F_LOCAL_SITU_ROWS = 8;
-static_assert(F_LOCAL_SITU_ROWS * (F_SH / 8) <= F_WORKERS, "one act chunk a thread");
+constexpr int F_ACT_CHUNKS = (F_LOCAL_SITU_ROWS * (F_SH / 8) + F_WORKERS - 1) / F_WORKERS;  // a thread
+static_assert(F_ACT_CHUNKS <= 2, "at most two act chunks a thread");
 static_assert(F_RANK_WARPS >= 2 && F_SORT_WARPS <= 31 && F_SORT_WARPS >= TOPK,
               "ranking warps, a warp left for the SiTU, at least TOPK warp maxima");
 static_assert(F_SH % 64 == 0 && F_NSH % 64 == 0 && F_LDS % 4 == 0, "whole swizzle atoms, 16-byte rows");
@@ -1066,17 +1069,20 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
   bf16* tile = reinterpret_cast<bf16*>(sa + F_OPERAND);               // out [T][64]
   const u32 sw_at = smem_u32(sw), sa_at = smem_u32(sa);
   // Few rows: every block computes the act rows itself from the front GEMM's gate | up (bit for bit as the
-  // row blocks do), one 8-column chunk a thread, its loads in flight before anything else
+  // row blocks do), 8-column chunks (t + m F_WORKERS), their loads in flight before anything else
   const bool local_act = T <= F_LOCAL_SITU_ROWS;
-  const int ar = t / (F_SH / 8), ak = t % (F_SH / 8);
-  const bool my_chunk = local_act && t < T * (F_SH / 8);
-  float4 g0 = make_float4(0.f, 0.f, 0.f, 0.f), g1 = g0, u0 = g0, u1 = g0;
-  if (my_chunk) {
-    const float* gp = S + (long long)ar * F_LDS + F_EXPERTS + LATENT + ak * 8;
-    g0 = reinterpret_cast<const float4*>(gp)[0];
-    g1 = reinterpret_cast<const float4*>(gp)[1];
-    u0 = reinterpret_cast<const float4*>(gp + F_SH)[0];
-    u1 = reinterpret_cast<const float4*>(gp + F_SH)[1];
+  float4 g0[F_ACT_CHUNKS], g1[F_ACT_CHUNKS], u0[F_ACT_CHUNKS], u1[F_ACT_CHUNKS];
+#pragma unroll
+  for (int m = 0; m < F_ACT_CHUNKS; ++m) {
+    const int i = t + m * F_WORKERS, ar = i / (F_SH / 8), ak = i % (F_SH / 8);
+    g0[m] = g1[m] = u0[m] = u1[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (local_act && i < T * (F_SH / 8)) {
+      const float* gp = S + (long long)ar * F_LDS + F_EXPERTS + LATENT + ak * 8;
+      g0[m] = reinterpret_cast<const float4*>(gp)[0];
+      g1[m] = reinterpret_cast<const float4*>(gp)[1];
+      u0[m] = reinterpret_cast<const float4*>(gp + F_SH)[0];
+      u1[m] = reinterpret_cast<const float4*>(gp + F_SH)[1];
+    }
   }
   if (warp == 1) {
     tmem_alloc(&s_tmem, 64);
@@ -1096,10 +1102,14 @@ extern "C" __global__ void __launch_bounds__(dropin::F_THREADS, 1) kern_k3_moe_f
   }
   front_work_sync();
   if (local_act) {
-    if (my_chunk)
-      *reinterpret_cast<uint4*>(sa + front_swizzle(ar, ak)) =
-          make_uint4(situ_bf16x2(g0.x, g0.y, u0.x, u0.y), situ_bf16x2(g0.z, g0.w, u0.z, u0.w),
-                     situ_bf16x2(g1.x, g1.y, u1.x, u1.y), situ_bf16x2(g1.z, g1.w, u1.z, u1.w));
+#pragma unroll
+    for (int m = 0; m < F_ACT_CHUNKS; ++m) {
+      const int i = t + m * F_WORKERS, ar = i / (F_SH / 8), ak = i % (F_SH / 8);
+      if (i < T * (F_SH / 8))
+        *reinterpret_cast<uint4*>(sa + front_swizzle(ar, ak)) =
+            make_uint4(situ_bf16x2(g0[m].x, g0[m].y, u0[m].x, u0[m].y), situ_bf16x2(g0[m].z, g0[m].w, u0[m].z, u0[m].w),
+                       situ_bf16x2(g1[m].x, g1[m].y, u1[m].x, u1[m].y), situ_bf16x2(g1[m].z, g1[m].w, u1[m].z, u1[m].w));
+    }
     cp_async_wait_all();
   } else {
     if (t < T) {
