@@ -778,7 +778,7 @@ EpPeerLayout ep_peer_layout(const k3moe_ep_config& c) {
 
 enum { EW_EPOCH, EW_ERR, EW_OWNER, EW_LOCAL, EW_IDX, EW_WTS, EW_DEST, EW_LID, EW_SEND_POS, EW_PAIR_POS, EW_PAIR_BACK,
        EW_ROWS_TO, EW_IDS, EW_COUNTS, EW_CTA_BATCH, EW_CTA_LIMIT, EW_META, EW_ROUTE_MAP, EW_EXP2PERM, EW_SCRATCH,
-       EW_QP, EW_SFP, EW_FC1Q, EW_FC1SF, EW_PTRS, EW_SHARED, EW_STAGE, EW_N };
+       EW_QP, EW_SFP, EW_FC1Q, EW_FC1SF, EW_PTRS, EW_SHARED, EW_N };
 
 struct EpWsLayout {
   size_t off[EW_N];
@@ -829,8 +829,6 @@ EpWsLayout ep_ws_layout(const k3moe_ep_config& c) {
   L.off[EW_FC1SF] = take((size_t)L.cap_rows * c.I / 32);
   L.off[EW_PTRS] = take((size_t)L.cap_rows * 8);
   L.off[EW_SHARED] = take((size_t)(T + 1) * c.H * 2);  // the last row: the sink of a bad return index
-  // the rows bound for each other rank, packed here and pushed to it as one contiguous run
-  L.off[EW_STAGE] = take(W > 1 ? (size_t)W * T * ep_peer_layout(c).stride : 0);
   L.total = at;
   return L;
 }
@@ -853,7 +851,6 @@ struct k3moe_ep {
   uint8_t* peer;
   const uint8_t *w13, *w13_sf, *w2, *w2_sf;
   EpBases recv_base;  // [d < W]: rank d's region of this rank's rows; [W]: this rank's shared region
-  EpBases pack_base;  // where the pack kernel writes: [me] and [W] as recv_base, [d != me] staging region d
   EpBases back_base;  // [s]: rank s's return buffer
   EpBases peer_base;  // [s]: rank s's peer buffer
   bool use_owner;
@@ -929,10 +926,6 @@ int k3moe_ep_create(const k3moe_ep_config* c, const int32_t* owner, const uint8_
     ep->peer_base.base[d] = peer_bases[d];
   }
   ep->recv_base.base[c->world] = peer_bases[c->rank] + (uint64_t)P.recv_off + (uint64_t)c->world * c->max_tokens * P.stride;
-  for (int d = 0; d <= c->world; ++d)
-    ep->pack_base.base[d] = d == c->rank || d == c->world
-                                ? ep->recv_base.base[d]
-                                : reinterpret_cast<uint64_t>(ws + L.off[EW_STAGE]) + (uint64_t)d * c->max_tokens * P.stride;
   *out = ep;
   return launch_status();
 }
@@ -972,14 +965,8 @@ int k3moe_ep_forward_events(k3moe_ep* ep, const float* S, int lds, const float* 
     const int tail = split == 1 ? (int)P.stride - H : 0;  // one warp a token: row tails in shared memory
     ep_pack_pairs_kernel<<<grid, 256, 8 * tail, s>>>(reinterpret_cast<const bf16*>(x_bf16), ldx, T, H, K,
                                                      I32(EW_DEST), I32(EW_LID), I32(EW_PAIR_POS), W, 0, nullptr,
-                                                     (int)P.stride, split, ep->pack_base, 1, c.shared ? L.El : -1,
+                                                     (int)P.stride, split, ep->recv_base, 1, c.shared ? L.El : -1,
                                                      I32(EW_PAIR_BACK), (int)P.back_col, tail);
-    if (W > 1) {  // the other ranks' rows, each rank's as one contiguous run
-      const int per_d = std::max(1, 4 * sms / (W - 1));
-      ep_push_kernel<<<per_d * (W - 1), 256, 0, s>>>(ep->recv_base, U8(EW_STAGE),
-                                                     (long long)c.max_tokens * P.stride, (int)P.stride, W, me,
-                                                     I32(EW_ROWS_TO));
-    }
   }
   ep_exchange_kernel<<<1, 32, 0, s>>>(ep->peer_base, P.counts_off, P.flags_off, W, me, 0, I32(EW_ROWS_TO), epoch,
                                       (unsigned long long)c.wait_budget_ns, err);

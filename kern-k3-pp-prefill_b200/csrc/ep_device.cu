@@ -209,23 +209,4 @@ __global__ void __launch_bounds__(256) ep_step_ptrs_kernel(const int* __restrict
   }
 }
 
-// The dispatch's remote half: the pack kernel wrote the rows bound for rank d (d != me) into this rank's local
-// staging region d (the layout of rank d's receive region `me`); blocks b with b % (W - 1) naming d copy
-// rows_to[d] rows of it to that region as contiguous 16-byte stores, so each peer's rows stream out as one
-// run instead of the pack's per-token interleaving across destinations.  Ends with a system-scope fence (the
-// exchange kernel that follows signals the peers).  gridDim.x a multiple of W - 1; W >= 2.
-__global__ void __launch_bounds__(256) ep_push_kernel(EpBases remote, const uint8_t* __restrict__ stage,
-                                                      long long region_bytes, int stride, int W, int me,
-                                                      const int* __restrict__ rows_to) {
-  const int lanes = W - 1;
-  const int q = blockIdx.x % lanes, d = q < me ? q : q + 1;
-  const int per_d = gridDim.x / lanes, k = blockIdx.x / lanes;
-  const long long units = (long long)rows_to[d] * stride / 16;
-  const uint4* src = reinterpret_cast<const uint4*>(stage + d * region_bytes);
-  uint4* dst = reinterpret_cast<uint4*>(remote.base[d]);
-  for (long long u = (long long)k * blockDim.x + threadIdx.x; u < units; u += (long long)per_d * blockDim.x)
-    dst[u] = src[u];
-  __threadfence_system();
-}
-
 }  // namespace k3

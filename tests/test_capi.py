@@ -129,10 +129,8 @@ def test_ep_step_buffer_sizes(lib):
     # the GEMM operands dominate: every pick a rank can receive (8 sources x 8192 tokens x 8 picks + the shared
     # rows), padded to 128 an expert, in MXFP8 (H + H/32) and FC1's output (I + I/32)
     cap = (112 + 1 + -(-(8 * 8192 * 8 + 8192) // 128)) * 128
-    # plus the staging of the rows bound for the other ranks (a region of max_tokens rows a rank)
-    stage = 8 * 8192 * stride
-    assert ws > cap * (7168 + 224 + 2048 + 64) + stage
-    assert ws < cap * (7168 + 224 + 2048 + 64 + 8) + stage + 2 ** 28
+    assert ws > cap * (7168 + 224 + 2048 + 64)
+    assert ws < cap * (7168 + 224 + 2048 + 64 + 8) + 2 ** 28
 
 
 def test_ep_step_rejects_bad_configurations_without_device_work(lib):
