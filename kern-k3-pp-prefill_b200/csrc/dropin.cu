@@ -675,6 +675,10 @@ constexpr int F_SITU_THREADS = F_SH / 4;        // 4 shared columns a thread
 constexpr int F_ATOM_COL = 64 * 128;            // 64 rows of 128-byte swizzle atoms
 constexpr int F_OPERAND = F_SH / 64 * F_ATOM_COL;
 constexpr int F_SMEM = 1024 + 2 * F_OPERAND + 64 * 64 * 2;
+// a row block's scratch in the dynamic shared memory: sigmoids, candidate keys and experts, warp maxima, picks,
+// the candidate count, per-warp counts, then the tables' expert masks, CTA offsets and CTA limits
+static_assert((3 * F_EXPERTS + 32 + 16 + 16 + 32) * 4 + F_LOCAL * 8 + (F_LOCAL + 1 + F_MAX_CTAS) * 4 <= F_SMEM,
+              "a row block's scratch fits the dynamic shared memory");
 constexpr int F_EPI_WARPS = F_WORKERS / 128 * 4;  // warps moving accumulator tiles out (whole lane quarters)
 constexpr long long F_FC1_W = 2LL * 3072 * (LATENT / 2), F_FC1_SF = 2LL * 3072 * (LATENT / 32);
 constexpr int F_ERR = 1 << 30, F_COUNT = 0xffff;
